@@ -1,0 +1,274 @@
+/*
+ * h3_oracle.c -- CPU restatement of the H3 DiT hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product links, loads or calls this
+ * file; only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+ * --impl reference legs use it, and there only as the checker or as the timed
+ * CPU baseline.
+ *
+ * Each function restates one step of the reference (paths are relative to the
+ * reference project root) in plain scalar C.  Every floating-point operation is
+ * a separate IEEE binary32 operation (this file is compiled with
+ * -ffp-contract=off); where the reference's GPU code performs a fused
+ * multiply-add the restatement calls fmaf() explicitly.
+ *
+ * Rounding switches.  The same routines also reproduce the reference kernels
+ * as Triton's CPU interpreter runs them, which is how the oracle is pinned to
+ * the reference's own code (tests/golden/make_golden.py):
+ *   final_round  H3O_RNE   float -> bf16 round-to-nearest-even (GPU, PyTorch)
+ *                H3O_TRUNC float -> bf16 truncation (Triton interpreter cast)
+ *   fma_sumsq    1: acc = fmaf(x, x, acc)   (nvcc / Triton GPU contraction)
+ *                0: acc = acc + x*x         (interpreter: two roundings)
+ *   rsqrt_mode   H3O_RSQRT_EXACT  correctly rounded 1/sqrt(v) (via double)
+ *                H3O_RSQRT_RECIP  1.0f / sqrtf(v)  (interpreter: 1/np.sqrt)
+ * The product semantics are (H3O_RNE, fma 1, EXACT) except that the GPU's
+ * rsqrtf() is an approximation (max 2 ulp); tests pass an rstd override to
+ * account for that, see h3o_norm_mod().
+ *
+ * Parity pin: bit-exact against the reference's Triton kernels
+ *   comfyui_nodes/h3-linear-fast/int8_gemm_triton.py:32-66 (_int8_mm_scaled_kernel)
+ *   comfyui_nodes/h3-fuse-graph/h3_fuse_kernels.py:88-167  (norm_mod, gate_norm_mod_, gate_)
+ * run under TRITON_INTERPRET=1 with (H3O_TRUNC, fma 0, RECIP) -- golden
+ * fixtures in tests/golden/.  The activation quantiser restates the formula
+ * the benchmark configuration states (per-token absmax / 127, half-even) --
+ * the reference's own quantiser is comfy-kitchen 0.2.39's compiled
+ * _C.quantize_int8_rowwise_convrot64, whose source is not in the reference,
+ * so that step is pinned only against the same formula evaluated by PyTorch.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define H3O_RNE 0
+#define H3O_TRUNC 1
+#define H3O_RSQRT_EXACT 0
+#define H3O_RSQRT_RECIP 1
+
+/* PyTorch's vectorized_layer_norm_kernel geometry that the reference's norm
+ * kernels imitate: 128 threads x 4-element vectors
+ * (h3_fuse_kernels.py:42-43). */
+#define H3O_NUMX 128
+#define H3O_VEC 4
+
+static inline float bf2f(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static inline uint32_t f2u(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+
+static inline float u2f(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* float -> bf16 bits.  RNE is the integer rounding of _rbf16
+ * (h3_fuse_kernels.py:78-85) and of PyTorch's c10::BFloat16 conversion;
+ * NaN maps to the quiet NaN 0x7FC0 with the input's sign. */
+static inline uint16_t f2bf(float f, int mode) {
+    uint32_t u = f2u(f);
+    if (mode == H3O_TRUNC) return (uint16_t)(u >> 16);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)(((u >> 16) & 0x8000u) | 0x7FC0u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+/* round a float to bf16 precision and keep it as float: _rbf16 */
+static inline float rbf16(float f) { return bf2f(f2bf(f, H3O_RNE)); }
+
+uint16_t h3o_f32_to_bf16(float f, int mode) { return f2bf(f, mode); }
+float h3o_bf16_to_f32(uint16_t b) { return bf2f(b); }
+
+/* ------------------------------------------------------------------------- */
+/* a1: per-token absmax activation quantisation.
+ * s[m] = absmax_k |x[m,k]| / 127  (IEEE binary32 division)
+ * q[m,k] = clamp(rint_half_even(x[m,k] / s[m]), -127, 127)
+ * A row whose absmax is 0 gets s = 0 and q = 0 (the formula would give 0/0).
+ * Replaces the call site comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:89-95. */
+void h3o_quant_rowwise(const uint16_t *x, int64_t M, int64_t K, int8_t *q, float *s) {
+    for (int64_t m = 0; m < M; ++m) {
+        const uint16_t *xr = x + m * K;
+        float amax = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            float a = fabsf(bf2f(xr[k]));
+            if (a > amax) amax = a;
+        }
+        float sc = amax / 127.0f;
+        s[m] = sc;
+        int8_t *qr = q + m * K;
+        if (sc == 0.0f) {
+            memset(qr, 0, (size_t)K);
+            continue;
+        }
+        for (int64_t k = 0; k < K; ++k) {
+            float r = nearbyintf(bf2f(xr[k]) / sc); /* default FE_TONEAREST: half-even */
+            if (r > 127.0f) r = 127.0f;
+            if (r < -127.0f) r = -127.0f;
+            qr[k] = (int8_t)r;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* a2: int8 x int8 -> int32 GEMM with the fp32 dequant epilogue.
+ * acc[m,n] = sum_k xq[m,k] * w[n,k]                (int32, exact)
+ * y[m,n]   = bf16((float(acc) * xs[m]) * ws[n])     int8_gemm_triton.py:2,61-66
+ * With a bias the fp32 value gets "+ float(bias[n])" before the single bf16
+ * rounding (the reference's fast path has no bias; its eligibility check at
+ * h3_linear_fast_patch.py:151 sends bias calls back to comfy-kitchen).
+ * acc_out (optional) receives the raw int32 accumulators. */
+void h3o_int8_mm_scaled(const int8_t *xq, const int8_t *w, const float *xs, const float *ws,
+                        const uint16_t *bias, int64_t M, int64_t N, int64_t K, uint16_t *y,
+                        int32_t *acc_out, int final_round) {
+    for (int64_t m = 0; m < M; ++m) {
+        const int8_t *a = xq + m * K;
+        for (int64_t n = 0; n < N; ++n) {
+            const int8_t *b = w + n * K;
+            int32_t acc = 0;
+            for (int64_t k = 0; k < K; ++k) acc += (int32_t)a[k] * (int32_t)b[k];
+            if (acc_out) acc_out[m * N + n] = acc;
+            float c = (float)acc * xs[m];
+            c = c * ws[n];
+            if (bias) c = c + bf2f(bias[n]);
+            y[m * N + n] = f2bf(c, final_round);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* a4: the row sum of squares in the reference's order.
+ * Thread t of 128 accumulates elements (it*128 + t)*4 + v for it = 0.. and
+ * v = 0..3 in that order (h3_fuse_kernels.py:98-102, _sumsq4 :55-62); masked
+ * tail elements contribute 0.  The 128 partials are then reduced per warp by
+ * the shuffle-down tree (lane i += lane i+16, +8, +4, +2, +1) and across the
+ * four warps as (w0 + w2) + (w1 + w3) (_tree128 :65-75).  x holds the row
+ * values already widened to float. */
+float h3o_row_sumsq(const float *x, int64_t D, int fma_sumsq) {
+    float acc[H3O_NUMX];
+    int64_t iters = ((D + H3O_VEC - 1) / H3O_VEC + H3O_NUMX - 1) / H3O_NUMX;
+    for (int t = 0; t < H3O_NUMX; ++t) {
+        float a = 0.0f;
+        for (int64_t it = 0; it < iters; ++it) {
+            for (int v = 0; v < H3O_VEC; ++v) {
+                int64_t idx = (it * H3O_NUMX + t) * H3O_VEC + v;
+                float xv = idx < D ? x[idx] : 0.0f;
+                if (fma_sumsq)
+                    a = fmaf(xv, xv, a);
+                else {
+                    float p = xv * xv;
+                    a = a + p;
+                }
+            }
+        }
+        acc[t] = a;
+    }
+    float wsum[4];
+    for (int w = 0; w < 4; ++w) {
+        float s[32];
+        for (int i = 0; i < 32; ++i) s[i] = acc[w * 32 + i];
+        for (int off = 16; off >= 1; off >>= 1)
+            for (int i = 0; i < off; ++i) s[i] = s[i] + s[i + off];
+        wsum[w] = s[0];
+    }
+    float lo = wsum[0] + wsum[2];
+    float hi = wsum[1] + wsum[3];
+    return lo + hi;
+}
+
+/* rstd = rsqrt(tot / D + eps)  (h3_fuse_kernels.py:104: div_rn, then rsqrt) */
+float h3o_rstd(float tot, int64_t D, float eps, int rsqrt_mode) {
+    float var = tot / (float)D;
+    float v = var + eps;
+    if (rsqrt_mode == H3O_RSQRT_RECIP) {
+        float r = sqrtf(v);
+        return 1.0f / r;
+    }
+    return (float)(1.0 / sqrt((double)v));
+}
+
+/* y = bf16(rbf16(rbf16(w * (rstd * x)) * s1) + sh) for one element
+ * (h3_fuse_kernels.py:110-114). */
+static inline uint16_t norm_mod_elem(float xv, float rstd, float wv, float s1v, float shv, int final_round) {
+    float t = rstd * xv;
+    float y = rbf16(wv * t);
+    y = rbf16(y * s1v);
+    float hsum = y + shv;
+    return f2bf(hsum, final_round);
+}
+
+/* a4: norm_mod(x, w, eps, ridx, s1, sh) -> h   (h3_fuse_kernels.py:88-114,174-178)
+ * x [S,D] bf16, w [D] bf16, ridx [S] int32 rows of the [R,D] tables s1 / sh,
+ * h [S,D] bf16.  rstd_override (optional, [S]) replaces the computed rstd of
+ * each row; rstd_out (optional, [S]) receives the rstd that was used. */
+void h3o_norm_mod(const uint16_t *x, const uint16_t *w, float eps, const int32_t *ridx,
+                  const uint16_t *s1, const uint16_t *sh, uint16_t *h, int64_t S, int64_t D,
+                  const float *rstd_override, float *rstd_out, int fma_sumsq, int rsqrt_mode,
+                  int final_round, float *rowbuf /* scratch [D] */) {
+    for (int64_t r = 0; r < S; ++r) {
+        const uint16_t *xr = x + r * D;
+        for (int64_t k = 0; k < D; ++k) rowbuf[k] = bf2f(xr[k]);
+        float rstd = rstd_override ? rstd_override[r]
+                                   : h3o_rstd(h3o_row_sumsq(rowbuf, D, fma_sumsq), D, eps, rsqrt_mode);
+        if (rstd_out) rstd_out[r] = rstd;
+        int64_t tr = ridx[r];
+        const uint16_t *s1r = s1 + tr * D, *shr = sh + tr * D;
+        for (int64_t k = 0; k < D; ++k)
+            h[r * D + k] = norm_mod_elem(rowbuf[k], rstd, bf2f(w[k]), bf2f(s1r[k]), bf2f(shr[k]), final_round);
+    }
+}
+
+/* residual x + o*g in fp32.  o and g are bf16, so o*g is exact in binary32 and
+ * the GPU's fused multiply-add (Triton fuses "x + o * g"; PyTorch's addcmul
+ * computes a + alpha*(b*c) in float) rounds once, like this mul-then-add. */
+static inline float gate_elem(float xv, float ov, float gv) {
+    float p = ov * gv;
+    return xv + p;
+}
+
+/* a5: gate_norm_mod_(x, o, g, w, eps, ridx, s1, sh) -> h, x updated in place
+ * xn = rbf16(x + o*g[r]); x <- xn; h = norm_mod(xn)  (h3_fuse_kernels.py:117-155,181-185) */
+void h3o_gate_norm_mod_(uint16_t *x, const uint16_t *o, const uint16_t *g, const uint16_t *w, float eps,
+                        const int32_t *ridx, const uint16_t *s1, const uint16_t *sh, uint16_t *h, int64_t S,
+                        int64_t D, const float *rstd_override, float *rstd_out, int fma_sumsq,
+                        int rsqrt_mode, int final_round, float *rowbuf /* scratch [D] */) {
+    for (int64_t r = 0; r < S; ++r) {
+        uint16_t *xr = x + r * D;
+        const uint16_t *orow = o + r * D;
+        int64_t tr = ridx[r];
+        const uint16_t *gr = g + tr * D;
+        for (int64_t k = 0; k < D; ++k) rowbuf[k] = rbf16(gate_elem(bf2f(xr[k]), bf2f(orow[k]), bf2f(gr[k])));
+        float rstd = rstd_override ? rstd_override[r]
+                                   : h3o_rstd(h3o_row_sumsq(rowbuf, D, fma_sumsq), D, eps, rsqrt_mode);
+        if (rstd_out) rstd_out[r] = rstd;
+        const uint16_t *s1r = s1 + tr * D, *shr = sh + tr * D;
+        for (int64_t k = 0; k < D; ++k) {
+            xr[k] = f2bf(rowbuf[k], final_round); /* rowbuf already holds a bf16 value */
+            h[r * D + k] = norm_mod_elem(rowbuf[k], rstd, bf2f(w[k]), bf2f(s1r[k]), bf2f(shr[k]), final_round);
+        }
+    }
+}
+
+/* a6: gate_(x, o, g, ridx): x <- bf16(x + o*g[r]) in place (h3_fuse_kernels.py:158-167,188-192) */
+void h3o_gate_(uint16_t *x, const uint16_t *o, const uint16_t *g, const int32_t *ridx, int64_t S, int64_t D,
+               int final_round) {
+    for (int64_t r = 0; r < S; ++r) {
+        const uint16_t *gr = g + (int64_t)ridx[r] * D;
+        for (int64_t k = 0; k < D; ++k)
+            x[r * D + k] = f2bf(gate_elem(bf2f(x[r * D + k]), bf2f(o[r * D + k]), bf2f(gr[k])), final_round);
+    }
+}
+
+/* a7: modulation table s1 = bf16(1.0 + scale) for bf16 scale (h3_fuse_patch.py:111-118) */
+void h3o_one_plus(const uint16_t *scale, uint16_t *out, int64_t n, int final_round) {
+    for (int64_t i = 0; i < n; ++i) {
+        float one = 1.0f;
+        out[i] = f2bf(one + bf2f(scale[i]), final_round);
+    }
+}
