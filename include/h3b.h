@@ -1,0 +1,170 @@
+/*
+ * h3b.h -- C ABI of libh3b, the B200 (sm_100a) implementation of the H3 video
+ * DiT hot path: INT8 linear, fused RMSNorm/adaLN/gate chain, Ulysses
+ * sequence<->head all-to-all.
+ *
+ * Conventions
+ *   - Plain device pointers and sizes; no framework types.  bf16 tensors are
+ *     passed as `void*` to 16-bit storage.  All tensors are row-major and
+ *     contiguous unless a leading dimension is given.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every entry
+ *     point only enqueues work; none synchronises unless stated.
+ *   - The caller owns every buffer: outputs and scratch are allocated by the
+ *     caller (the Python host uses PyTorch's caching allocator), and the
+ *     library never frees caller memory.
+ *   - Return value: H3B_OK (0) or a negative H3B_ERR_* code;
+ *     h3b_last_error() describes the last failure on the calling thread.
+ *   - Kernels that wait (mbarrier pipelines, peer flags) give up after a
+ *     bounded time and record an H3B_STATUS_* code in a device status word;
+ *     read it with h3b_status_get().
+ *
+ * Reference interfaces cited as path:line inside the reference project
+ * (yuichi-suzuki-highdrama/minimax-h3-multi-dgx-spark).
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3B_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define H3B_API __attribute__((visibility("default")))
+#else
+#define H3B_API
+#endif
+
+#define H3B_OK 0
+#define H3B_ERR_ARG (-1)         /* bad shape, stride, alignment or pointer */
+#define H3B_ERR_CUDA (-2)        /* a CUDA runtime/driver call failed */
+#define H3B_ERR_UNSUPPORTED (-3) /* not an sm_100 device, or a size the kernels do not cover */
+
+#define H3B_STATUS_OK 0
+#define H3B_STATUS_MBAR_TIMEOUT 1 /* a GEMM pipeline wait ran out (kernel aborted its tile loop) */
+#define H3B_STATUS_PEER_TIMEOUT 2 /* a peer barrier wait ran out (a rank did not arrive) */
+#define H3B_STATUS_BAD_INDEX 3    /* a modulation row index was outside [0, R) (row skipped) */
+
+H3B_API int h3b_abi_version(void);
+H3B_API const char *h3b_last_error(void);
+
+/* Device status word of the current device.  h3b_status_get synchronises
+ * `stream` first, then reads the word; h3b_status_clear resets it to 0. */
+H3B_API int h3b_status_get(int *status_out, void *stream);
+H3B_API int h3b_status_clear(void *stream);
+
+/* ---- INT8 linear ------------------------------------------------------- */
+
+/* Per-token absmax activation quantisation (row m of x, leading dimension ldx
+ * elements): xs[m] = max_k |x[m,k]| / 127 (IEEE fp32 division);
+ * xq[m,k] = clamp(rint_half_even(x[m,k] / xs[m]), -127, 127); an all-zero row
+ * gives xs = 0 and xq = 0.  x bf16 [M,K]; xq int8 [M,K]; xs fp32 [M].
+ * K % 8 == 0, K <= 32768, x and ldx 16-byte aligned.
+ * Replaces comfy-kitchen's _C.quantize_int8_rowwise_convrot64 at the call site
+ * comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:89-95 (the formula is
+ * the plain per-token absmax quantiser; the ConvRot rotation is not applied). */
+H3B_API int h3b_quant_rowwise(const void *x, int64_t ldx, int64_t M, int64_t K, int8_t *xq, float *xs, void *stream);
+
+/* INT8 GEMM with dequant epilogue on tcgen05 tensor cores:
+ * acc[m,n] = sum_k xq[m,k] * w[n,k] (int32), out[m,n] =
+ * bf16((float(acc) * xs[m]) * ws[n] [+ float(bias[n])]) with one rounding.
+ * xq int8 [M,K], w int8 [N,K] (both K-contiguous), xs fp32 [M], ws fp32 [N],
+ * bias bf16 [N] or NULL, out bf16 [M,N].  K % 128 == 0, N % 8 == 0, all
+ * pointers 16-byte aligned.
+ * Replaces int8_mm_scaled, comfyui_nodes/h3-linear-fast/int8_gemm_triton.py:74-83
+ * (kernel :32-66; bias is an addition, NULL reproduces the reference formula). */
+H3B_API int h3b_int8_mm_scaled(const int8_t *xq, const int8_t *w, const float *xs, const float *ws, const void *bias,
+                       void *out, int64_t M, int64_t N, int64_t K, void *stream);
+
+/* Same GEMM writing the raw int32 accumulators acc [M,N] (the value the
+ * reference kernel's tl.dot produces, int8_gemm_triton.py:54-60). */
+H3B_API int h3b_int8_mm_i32(const int8_t *xq, const int8_t *w, int32_t *acc, int64_t M, int64_t N, int64_t K,
+                    void *stream);
+
+/* Patched Linear forward: quantise x (h3b_quant_rowwise) into the caller's
+ * scratch xq [M,K] / xs [M], then h3b_int8_mm_scaled into out [M,N].
+ * Replaces the patched comfy_kitchen.backends.cuda.int8_linear,
+ * comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:60-110. */
+H3B_API int h3b_int8_linear(const void *x, int64_t M, int64_t K, const int8_t *w, const float *ws, const void *bias,
+                    int64_t N, void *out, int8_t *xq_scratch, float *xs_scratch, void *stream);
+
+/* ---- fused RMSNorm / adaLN modulation / gate / residual ----------------- */
+/* x, o, h bf16 [S,D]; w bf16 [D]; ridx int32 [S] selects a row of the bf16
+ * modulation tables s1 / sh / g [R,D] (0 <= ridx < R is checked on the
+ * device: a row with an out-of-range index is skipped and recorded as
+ * H3B_STATUS_BAD_INDEX).  D % 4 == 0, D <= 16384,
+ * rows 8-byte aligned.  Sums of squares, the rsqrt and the bf16 rounding
+ * points follow the reference kernels bit for bit (rsqrtf as on the GPU). */
+
+/* h = bf16(rbf16(rbf16(w * (rstd * x)) * s1[r]) + sh[r]),
+ * rstd = rsqrt(sum(x^2) / D + eps).
+ * Replaces norm_mod, comfyui_nodes/h3-fuse-graph/h3_fuse_kernels.py:174-178 (kernel :88-114). */
+H3B_API int h3b_norm_mod(const void *x, const void *w, float eps, const int32_t *ridx, const void *s1, const void *sh,
+                 void *h, int64_t S, int64_t D, int64_t R, void *stream);
+
+/* x <- bf16(x + o * g[r]) in place, then h = norm_mod(x).
+ * Replaces gate_norm_mod_, h3_fuse_kernels.py:181-185 (kernel :117-155). */
+H3B_API int h3b_gate_norm_mod_(void *x, const void *o, const void *g, const void *w, float eps, const int32_t *ridx,
+                       const void *s1, const void *sh, void *h, int64_t S, int64_t D, int64_t R, void *stream);
+
+/* x <- bf16(x + o * g[r]) in place.
+ * Replaces gate_, h3_fuse_kernels.py:188-192 (kernel :158-167). */
+H3B_API int h3b_gate_(void *x, const void *o, const void *g, const int32_t *ridx, int64_t S, int64_t D, int64_t R,
+              void *stream);
+
+/* ---- Ulysses all-to-all -------------------------------------------------- */
+
+/* Forward pack: t [s_local, P * chunk] -> send [P, s_local, chunk]
+ * (chunk = (H/P)*Dh elements, given in bytes).  The NCCL exchange that
+ * follows receives [S, chunk] already in sequence order.
+ * Replaces t.reshape(s_local, p, chunk).transpose(0, 1).contiguous() of
+ * comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:185. */
+H3B_API int h3b_a2a_pack(const void *t, void *send, int64_t s_local, int64_t chunk_bytes, int world, void *stream);
+
+/* Inverse unpack: recv [P, s_local, chunk] -> out [s_local, P * chunk].
+ * Replaces out.view(p, s_local, chunk).transpose(0, 1).reshape(...) of
+ * sp_forward.py:198. */
+H3B_API int h3b_a2a_unpack(const void *recv, void *out, int64_t s_local, int64_t chunk_bytes, int world, void *stream);
+
+/* CUDA IPC plumbing for the peer-memory all-to-all.  h3b_ipc_handle returns
+ * the 64-byte cudaIpcMemHandle of the allocation holding dev_ptr and
+ * dev_ptr's offset inside it; h3b_ipc_open maps a peer's allocation and
+ * returns base + offset (and the base, for h3b_ipc_close). */
+H3B_API int h3b_ipc_handle(const void *dev_ptr, void *handle_out, int64_t *offset_out);
+H3B_API int h3b_ipc_open(const void *handle, int64_t offset, void **dev_ptr_out, void **base_out);
+H3B_API int h3b_ipc_close(void *base);
+
+/* Cross-rank barrier over peer memory: rank `rank` stores `epoch` into slot
+ * [rank] of every peer's flag array (peer_flags[j], uint32 [P]) with
+ * system-scope release, then waits until every slot of its own array
+ * (peer_flags[rank]) is >= epoch.  Gives up after timeout_ns and records
+ * H3B_STATUS_PEER_TIMEOUT.  Work before the barrier on `stream` (including
+ * peer-memory stores) is visible to every rank's work after it.
+ * Takes the place of the synchronisation inside the NCCL all_to_all_single
+ * calls of comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:164-166,174-176. */
+H3B_API int h3b_peer_barrier(uint32_t *const *peer_flags, int world, int rank, uint32_t epoch, int64_t timeout_ns,
+                     void *stream);
+
+/* Forward exchange fused with the pack, over peer memory: for each of n
+ * tensors src[i] [s_local, P * chunk] and each rank j, rows go straight into
+ * rank j's receive buffer dst[i * P + j] ([S, chunk]) at rows
+ * row_start .. row_start + s_local.  Bracket with h3b_peer_barrier.
+ * Replaces a2a_gather_seq_scatter_heads / _seq_gather, sp_forward.py:158-166,179-188. */
+H3B_API int h3b_a2a_fwd_p2p(int n, const void *const *src, void *const *dst, int64_t s_local, int64_t row_start,
+                    int64_t chunk_bytes, int world, void *stream);
+
+/* Inverse exchange fused with the unpack: src [S, chunk] rows (leading
+ * dimension src_ld bytes) split by `splits` (P entries) go to rank j's
+ * output dst[j] ([splits[j], P * chunk]) at column block `rank`.
+ * Replaces a2a_scatter_seq_gather_heads / _seq_scatter, sp_forward.py:169-176,191-198. */
+H3B_API int h3b_a2a_inv_p2p(const void *src, int64_t src_ld, void *const *dst, const int64_t *splits, int64_t chunk_bytes,
+                    int world, int rank, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */

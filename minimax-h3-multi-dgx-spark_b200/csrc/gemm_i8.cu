@@ -1,0 +1,486 @@
+// a2: INT8 x INT8 -> INT32 GEMM on 5th-generation tensor cores (tcgen05,
+// kind::i8) with the fp32 dequant (+bias) epilogue fused, for sm_100a.
+//
+//   out[m,n] = bf16((float(acc[m,n]) * xs[m]) * ws[n] [+ float(bias[n])])
+//   acc[m,n] = sum_k xq[m,k] * w[n,k]          (both operands K-contiguous)
+//
+// Design (one CTA per SM, persistent):
+//   warp 0      TMA producer: 128x128-byte A tiles and 256x128-byte B tiles,
+//               128B-swizzled, into a STAGES-deep shared-memory ring
+//               (no cluster multicast: each CTA loads its own tiles).
+//   warp 1      allocates 512 TMEM columns and issues the MMAs from one
+//               thread: 4 x tcgen05.mma M=128 N=256 K=32 per stage into one
+//               of two 256-column int32 accumulators; tcgen05.commit frees the
+//               stage and, after the last k-block, hands the accumulator over.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows), dequantise with separate
+//               IEEE multiplies (no FMA contraction: the reference rounds
+//               after each product), round once to bf16, store; then release
+//               the accumulator so the MMA warp can start the tile after next
+//               while this one drains.
+// Tiles are visited in the reference's grouped-M order (GROUP_M = 8,
+// int8_gemm_triton.py:37-45) so CTAs running at the same time share A and B
+// rows in L2.  Every mbarrier wait is bounded; on expiry the kernel records
+// H3B_STATUS_MBAR_TIMEOUT, stops issuing work, drains its own TMA loads and
+// MMAs (again bounded), frees TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace h3b {
+namespace gemm {
+
+constexpr int BM = 128;                  // tile rows (TMEM lanes)
+constexpr int BN = 256;                  // tile columns (TMEM columns per accumulator)
+constexpr int BK = 128;                  // k-block in bytes = one 128B swizzle row
+constexpr int UMMA_K = 32;               // K per kind::i8 instruction
+constexpr int STAGES = 4;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512: the whole TMEM of the SM
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int GROUP_M = 8;
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr uint64_t kTimeoutNs = 10ull * 1000 * 1000 * 1000;
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+
+// Instruction descriptor: D s32 (bits 4-5 = 2), A s8 (7-9 = 1), B s8 (10-12 = 1),
+// both K-major (bits 15/16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+struct Args {
+    const float* xs;
+    const float* ws;
+    const uint16_t* bias;
+    void* out;
+    int M, N, K;
+    int* status;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  Returns false
+// if the kernel is aborting (another role timed out) or this wait timed out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          uint64_t limit_ns = kTimeoutNs) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((n & 127u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > limit_ns) {
+                *abort_flag = 1;
+                report(status, H3B_STATUS_MBAR_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: start address
+// >> 4 (bits 0-13), leading byte offset 16 B (unused with swizzle), stride
+// byte offset 1024 B = 8 rows x 128 B (bits 32-45), descriptor version 1
+// (bit 46), layout SWIZZLE_128B = 2 (bits 61-63).  Stepping K by 32 bytes
+// inside the 128-byte swizzle row advances the start address; the hardware
+// applies the XOR swizzle to the final address, matching TMA's layout.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
+    const int in_group = GROUP_M * n_tiles;
+    const int group = tile / in_group;
+    const int first_m = group * GROUP_M;
+    const int gsize = min(m_tiles - first_m, GROUP_M);
+    const int r = tile % in_group;
+    mb = first_m + r % gsize;
+    nb = r / gsize;
+}
+
+// ---------------------------------------------------------------------------
+
+template <bool OUT_I32>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = base;
+    uint8_t* sB = base + STAGES * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + NUM_ACC;
+    uint64_t* drain = tempty + NUM_ACC;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < NUM_ACC; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int M = args.M, N = args.N, K = args.K;
+    const int m_tiles = (M + BM - 1) / BM, n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = m_tiles * n_tiles;
+    const int kblocks = K / BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            int armed = 0;  // loads issued (bounded drain below needs the last STAGES)
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                int mb, nb;
+                tile_coords(tile, m_tiles, n_tiles, mb, nb);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[stage], STAGE_BYTES);
+                    tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
+                    tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+                    ++armed;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let the loads this thread issued land before the CTA exits:
+                // walk back over the last (up to STAGES) armed stages.
+                int s = stage;
+                uint32_t p = phase;
+                for (int i = 0; i < STAGES && i < armed; ++i) {
+                    if (--s < 0) {
+                        s = STAGES - 1;
+                        p ^= 1u;
+                    }
+                    volatile int no_abort = 0;
+                    mbar_wait(&full[s], p, &no_abort, nullptr, 100ull * 1000 * 1000);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer
+            int stage = 0;
+            uint32_t phase = 0;
+            int t = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++t) {
+                const int acc = t & 1;
+                const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
+                        umma_i8(d_tmem, smem_desc(a0 + kk * UMMA_K), smem_desc(b0 + kk * UMMA_K), (kb | kk) != 0);
+                    issued = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) umma_commit(&tfull[acc]);
+            }
+            if (!ok && issued) {
+                // Wait (bounded) until every MMA this thread issued has finished.
+                umma_commit(drain);
+                volatile int no_abort = 0;
+                mbar_wait(drain, 0, &no_abort, nullptr, 100ull * 1000 * 1000);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..5
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int t = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+            int mb, nb;
+            tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            const int acc = t & 1;
+            const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status)) break;
+            tc_fence_after();
+            const int row = mb * BM + q * 32 + lane;
+            const bool row_ok = row < M;
+            float xs = 0.0f;
+            if constexpr (!OUT_I32) xs = row_ok ? args.xs[row] : 0.0f;
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = nb * BN + c * 32;
+                if (col0 >= N) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld32(t_row + (uint32_t)(c * 32), r);
+                if (!row_ok) continue;
+                if constexpr (OUT_I32) {
+                    int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(args.out) + (int64_t)row * N + col0);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        if (col0 + 4 * g < N)
+                            dst[g] = make_int4((int)r[4 * g], (int)r[4 * g + 1], (int)r[4 * g + 2], (int)r[4 * g + 3]);
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + (int64_t)row * N + col0);
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int cb = col0 + 8 * g;
+                        if (cb >= N) break;
+                        const float4 w0 = *reinterpret_cast<const float4*>(args.ws + cb);
+                        const float4 w1 = *reinterpret_cast<const float4*>(args.ws + cb + 4);
+                        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                        float bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                        if (args.bias) {
+                            const uint4 b = *reinterpret_cast<const uint4*>(args.bias + cb);
+                            const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                bv[2 * e] = bf16_lo(bu[e]);
+                                bv[2 * e + 1] = bf16_hi(bu[e]);
+                            }
+                        }
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            float v0 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e]), xs), wv[2 * e]);
+                            float v1 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e + 1]), xs), wv[2 * e + 1]);
+                            if (args.bias) {
+                                v0 = __fadd_rn(v0, bv[2 * e]);
+                                v1 = __fadd_rn(v1, bv[2 * e + 1]);
+                            }
+                            o[e] = pack_bf16x2(v0, v1);
+                        }
+                        dst[g] = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled encode_fn() {
+    static PFN_encodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+    }
+    return fn;
+}
+
+// 2-D int8 tensor [rows, K] (K contiguous) tiled as box_rows x 128 bytes, 128B swizzle.
+static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, uint32_t box_rows) {
+    PFN_encodeTiled enc = encode_fn();
+    if (!enc) return set_error(H3B_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (driver too old?)");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K};
+    cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(H3B_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return H3B_OK;
+}
+
+static int num_sms() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return sms;
+}
+
+static int check_device() {
+    int dev = 0, major = 0;
+    H3B_CUDA_TRY(cudaGetDevice(&dev));
+    H3B_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return set_error(H3B_ERR_UNSUPPORTED, "libh3b GEMM needs an sm_100 GPU (found compute %d.x)", major);
+    return H3B_OK;
+}
+
+template <bool OUT_I32>
+static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
+    H3B_REQUIRE(xq && w && a.out, "h3b GEMM: NULL pointer");
+    H3B_REQUIRE(a.M >= 0 && a.N > 0 && a.K > 0, "h3b GEMM: bad shape M=%d N=%d K=%d", a.M, a.N, a.K);
+    H3B_REQUIRE(a.K % BK == 0, "h3b GEMM: K=%d must be a multiple of %d", a.K, BK);
+    H3B_REQUIRE(a.N % 8 == 0, "h3b GEMM: N=%d must be a multiple of 8", a.N);
+    H3B_REQUIRE(aligned(xq, 16) && aligned(w, 16) && aligned(a.out, 16), "h3b GEMM: operands must be 16-byte aligned");
+    if (!OUT_I32) {
+        H3B_REQUIRE(a.xs && a.ws && aligned(a.ws, 16), "h3b GEMM: xs/ws NULL or ws not 16-byte aligned");
+        H3B_REQUIRE(!a.bias || aligned(a.bias, 16), "h3b GEMM: bias must be 16-byte aligned");
+    }
+    if (a.M == 0) return H3B_OK;
+    if (int rc = check_device()) return rc;
+    CUtensorMap tmA, tmB;
+    if (int rc = make_map(&tmA, xq, a.M, a.K, BM)) return rc;
+    if (int rc = make_map(&tmB, w, a.N, a.K, BN)) return rc;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    a.status = ds.word;
+    H3B_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+    const int64_t tiles = (int64_t)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+    const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+    gemm_i8_kernel<OUT_I32><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, a);
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
+}
+
+}  // namespace gemm
+
+int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs, cudaStream_t s);
+
+}  // namespace h3b
+
+using namespace h3b;
+
+static bool fits_int(int64_t v) { return v >= 0 && v < (1ll << 31); }
+
+extern "C" int h3b_int8_mm_scaled(const int8_t* xq, const int8_t* w, const float* xs, const float* ws,
+                                  const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+    H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_scaled: shape out of range");
+    gemm::Args a{xs, ws, static_cast<const uint16_t*>(bias), out, (int)M, (int)N, (int)K, nullptr};
+    return gemm::launch<false>(xq, w, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_int8_mm_i32(const int8_t* xq, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                               void* stream) {
+    H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_i32: shape out of range");
+    gemm::Args a{nullptr, nullptr, nullptr, acc, (int)M, (int)N, (int)K, nullptr};
+    return gemm::launch<true>(xq, w, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_int8_linear(const void* x, int64_t M, int64_t K, const int8_t* w, const float* ws,
+                               const void* bias, int64_t N, void* out, int8_t* xq_scratch, float* xs_scratch,
+                               void* stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    H3B_REQUIRE(K % gemm::BK == 0, "h3b_int8_linear: K=%lld must be a multiple of %d", (long long)K, gemm::BK);
+    if (int rc = quant_rowwise(x, K, M, K, xq_scratch, xs_scratch, s)) return rc;
+    return h3b_int8_mm_scaled(xq_scratch, w, xs_scratch, ws, bias, out, M, N, K, stream);
+}

@@ -1,0 +1,20 @@
+"""h3b -- B200-native (sm_100a) H3 video-DiT hot path.
+
+Drop-in replacements for the three hooks of yuichi-suzuki-highdrama/minimax-h3-multi-dgx-spark:
+  * INT8 linear            h3b.linear   (h3-linear-fast)
+  * fused norm/mod/gate    h3b.fuse     (h3-fuse-graph)
+  * Ulysses all-to-all     h3b.sp       (minimax-h3-sp)
+All compute runs in libh3b.so (hand-written CUDA for sm_100a, C ABI in
+include/h3b.h); this package is the host-side mirror of the reference's
+operator interfaces.  Importing it fails if the library is not built.
+"""
+from ._lib import H3BError, clear_status, lib, status  # noqa: F401
+from .fuse import gate_, gate_norm_mod_, modulation_tables, norm_mod, row_index  # noqa: F401
+from .linear import int8_linear, int8_mm_i32, int8_mm_scaled, linear, quant_rowwise, supported  # noqa: F401
+from .sp import (PeerExchange, SPContext, a2a_gather_qkv, a2a_gather_seq_scatter_heads,  # noqa: F401
+                 a2a_scatter_seq_gather_heads, pack, startup_probe, unpack)
+
+__all__ = ["H3BError", "status", "clear_status", "norm_mod", "gate_norm_mod_", "gate_", "row_index",
+           "modulation_tables", "quant_rowwise", "int8_mm_scaled", "int8_mm_i32", "int8_linear", "linear",
+           "supported", "SPContext", "PeerExchange", "a2a_gather_seq_scatter_heads", "a2a_scatter_seq_gather_heads",
+           "a2a_gather_qkv", "pack", "unpack", "startup_probe"]

@@ -1,0 +1,104 @@
+"""INT8 linear ops (activation quantiser, GEMM + dequant, patched Linear) over libh3b.
+
+Mirrors the reference's operator surface:
+  int8_mm_scaled(xq, w, xs, ws, out=None)    comfyui_nodes/h3-linear-fast/int8_gemm_triton.py:74-83
+  supported(K)                               int8_gemm_triton.py:86-87
+  int8_linear(x, weight, weight_scale, ...)  the patched comfy_kitchen int8_linear,
+                                             comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:60-110
+Outputs are allocated with PyTorch's caching allocator on the input's device,
+kernels run on the current CUDA stream, shape/dtype violations raise.
+"""
+import torch
+
+from ._lib import check, lib, ptr, require_cuda, stream_of
+
+
+def supported(K):
+    """K the GEMM accepts: a multiple of the 128-byte k-block (the reference needs K % 128 == 0 too)."""
+    return K % 128 == 0
+
+
+def quant_rowwise(x, xq=None, xs=None):
+    """Per-token absmax quantisation: x bf16 [M,K] -> (xq int8 [M,K], xs fp32 [M,1]).
+
+    xs = absmax/127, xq = clamp(round_half_even(x/xs), -127, 127); zero rows give 0/0.
+    The [M,1] scale shape follows the reference's x_s (h3_linear_fast_patch.py:91)."""
+    require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError(f"quant_rowwise: x must be a 2-D bf16 tensor with unit column stride, got {x.dtype} {tuple(x.shape)}")
+    M, K = x.shape
+    if xq is None:
+        xq = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    if xs is None:
+        xs = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    check(lib.h3b_quant_rowwise(ptr(x), x.stride(0), M, K, ptr(xq), ptr(xs), stream_of(x)), "h3b_quant_rowwise")
+    return xq, xs
+
+
+def _gemm_checks(xq, w):
+    require_cuda(xq, w)
+    if xq.dtype != torch.int8 or w.dtype != torch.int8 or xq.dim() != 2 or w.dim() != 2:
+        raise ValueError("int8 GEMM: xq and w must be 2-D int8 tensors")
+    M, K = xq.shape
+    N = w.shape[0]
+    assert w.shape[1] == K and xq.is_contiguous() and w.is_contiguous()
+    return M, N, K
+
+
+def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
+    """xq [M,K] int8, w [N,K] int8, xs [M,1] fp32, ws [N] fp32 -> [M,N] bf16.
+
+    out = bf16((float(xq @ w.T) * xs) * ws [+ bias]) with one rounding."""
+    M, N, K = _gemm_checks(xq, w)
+    xs = xs.reshape(-1)
+    if xs.dtype != torch.float32 or ws.dtype != torch.float32 or xs.numel() != M or ws.numel() != N:
+        raise ValueError("int8_mm_scaled: xs must be fp32 [M] / [M,1] and ws fp32 [N]")
+    xs, ws = xs.contiguous(), ws.contiguous()
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != N:
+            raise ValueError("int8_mm_scaled: bias must be bf16 [N]")
+        bias = bias.contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
+    check(lib.h3b_int8_mm_scaled(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
+          "h3b_int8_mm_scaled")
+    return out
+
+
+def int8_mm_i32(xq, w, out=None):
+    """Raw int32 accumulators xq @ w.T (for bit-exact checks of the tensor-core path)."""
+    M, N, K = _gemm_checks(xq, w)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.int32, device=xq.device)
+    check(lib.h3b_int8_mm_i32(ptr(xq), ptr(w), ptr(out), M, N, K, stream_of(xq)), "h3b_int8_mm_i32")
+    return out
+
+
+def linear(x, w, ws, bias=None):
+    """The INT8 linear on a [*, K] bf16 activation: per-token quant + GEMM + dequant(+bias)."""
+    kin = x.shape[-1]
+    x2d = x.reshape(-1, kin)
+    if not x2d.is_contiguous():
+        x2d = x2d.contiguous()
+    xq, xs = quant_rowwise(x2d)
+    out = int8_mm_scaled(xq, w, xs, ws, bias=bias)
+    return out if x.dim() == 2 else out.reshape(*x.shape[:-1], w.shape[0])
+
+
+def int8_linear(x, weight, weight_scale, bias=None, out_dtype=None, convrot=False, convrot_groupsize=256,
+                input_act=None, input_act_weight=None, input_act_eps=0.0, residual=None, residual_scale=None):
+    """Signature of comfy_kitchen.backends.cuda.int8_linear (h3_linear_fast_patch.py:60-61).
+
+    Covers the plain per-token quantiser (convrot=False), no input activation and
+    no residual; anything else raises NotImplementedError so that an installer
+    can route the call to the original implementation, as the reference does
+    for ineligible calls (h3_linear_fast_patch.py:64-80)."""
+    if convrot or input_act not in (None, "none") or residual is not None:
+        raise NotImplementedError("h3b int8_linear: convrot / input_act / residual variants are not covered")
+    if (out_dtype or x.dtype) != torch.bfloat16 or x.dtype != torch.bfloat16:
+        raise NotImplementedError("h3b int8_linear: bf16 in/out only")
+    n = weight.shape[0]
+    ws = weight_scale.reshape(-1).to(torch.float32)
+    if ws.numel() != n:
+        ws = ws.expand(n).contiguous()
+    return linear(x, weight.contiguous(), ws, bias)

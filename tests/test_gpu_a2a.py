@@ -1,0 +1,101 @@
+"""GPU parity of the Ulysses all-to-all kernels on one GPU (bit-exact).
+
+Pack/unpack are checked against the numpy restatement of sp_forward.py:185/198.
+The peer-memory exchange kernels are checked by running every rank's launch on
+one GPU with all "peer" buffers local: the copy kernels never wait on anything,
+so this exercises their full index arithmetic without a second GPU.  The
+barrier kernel's bounded wait is checked by letting it wait for a flag that
+nothing sets.  Multi-GPU runs are in test_gpu_multi.py.
+"""
+import ctypes
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bits, randn_bf16
+from oracle import sp_layout
+
+pytestmark = pytest.mark.gpu
+
+h3b = pytest.importorskip("h3b")
+from h3b._lib import check, lib, ptr_array, STATUS_PEER_TIMEOUT  # noqa: E402
+
+DEV = "cuda"
+H, DH = 40, 128
+
+
+@pytest.mark.parametrize("world,s_local", [(2, 1000), (4, 333), (8, 16384), (1, 10)])
+def test_pack_unpack(world, s_local):
+    t = randn_bf16((s_local, H, DH), seed=world * 100 + s_local)
+    send = h3b.pack(t.to(DEV).reshape(s_local, H * DH), world)
+    ref = sp_layout.pack_fwd(bits(t), world)
+    np.testing.assert_array_equal(bits(send), ref)
+    back = h3b.unpack(send)
+    np.testing.assert_array_equal(bits(back), bits(t).reshape(s_local, H * DH))
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("world,S", [(2, 1001), (4, 4130), (8, 8192)])
+def test_p2p_kernels_emulated(world, S):
+    """Every rank's fwd/inv launch on one GPU against sp_layout.a2a_fwd / a2a_inv."""
+    splits = sp_layout.splits(S, world)
+    starts = sp_layout.starts(S, world)
+    hp = H // world
+    chunk = hp * DH
+    qs = [randn_bf16((splits[r], H, DH), seed=1000 + r) for r in range(world)]
+    ks = [randn_bf16((splits[r], H, DH), seed=2000 + r) for r in range(world)]
+    recv_q = [torch.empty(S, chunk, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+    recv_k = [torch.empty(S, chunk, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+    qd = [q.to(DEV) for q in qs]
+    kd = [k.to(DEV) for k in ks]
+    for r in range(world):
+        src, k1 = ptr_array([qd[r].data_ptr(), kd[r].data_ptr()])
+        dst, k2 = ptr_array([t.data_ptr() for t in recv_q] + [t.data_ptr() for t in recv_k])
+        check(lib.h3b_a2a_fwd_p2p(2, src, dst, splits[r], starts[r], chunk * 2, world, _stream()), "fwd_p2p")
+    torch.cuda.synchronize()
+    ref_q = sp_layout.a2a_fwd([bits(q) for q in qs], world)
+    ref_k = sp_layout.a2a_fwd([bits(k) for k in ks], world)
+    for j in range(world):
+        np.testing.assert_array_equal(bits(recv_q[j]).reshape(S, hp, DH), ref_q[j])
+        np.testing.assert_array_equal(bits(recv_k[j]).reshape(S, hp, DH), ref_k[j])
+    # inverse: rank j holds o_j [S, chunk] (use a strided view to exercise src_ld)
+    outs = [randn_bf16((S, chunk + 64), seed=3000 + j) for j in range(world)]
+    od = [o.to(DEV)[:, :chunk] for o in outs]
+    res = [torch.empty(splits[r], world * chunk, dtype=torch.bfloat16, device=DEV) for r in range(world)]
+    sp = (ctypes.c_int64 * world)(*splits)
+    for j in range(world):
+        dst, k3 = ptr_array([t.data_ptr() for t in res])
+        check(lib.h3b_a2a_inv_p2p(ctypes.c_void_p(od[j].data_ptr()), od[j].stride(0) * 2, dst, sp, chunk * 2, world, j,
+                                  _stream()), "inv_p2p")
+    torch.cuda.synchronize()
+    ref = sp_layout.a2a_inv([bits(o)[:, :chunk] for o in outs], world)
+    for r in range(world):
+        np.testing.assert_array_equal(bits(res[r]), ref[r])
+
+
+def test_peer_barrier_times_out_and_reports():
+    """A barrier whose peer never arrives gives up after its limit and records
+    STATUS_PEER_TIMEOUT; the context stays usable and an arrived barrier passes."""
+    world = 2
+    f0 = torch.zeros(world, dtype=torch.int32, device=DEV)
+    f1 = torch.zeros(world, dtype=torch.int32, device=DEV)
+    arr, keep = ptr_array([f0.data_ptr(), f1.data_ptr()])
+    h3b.clear_status()
+    t0 = time.time()
+    check(lib.h3b_peer_barrier(arr, world, 0, 1, int(0.3e9), _stream()), "barrier")
+    st = h3b.status()
+    elapsed = time.time() - t0
+    assert st == STATUS_PEER_TIMEOUT
+    assert elapsed < 10
+    assert f1[0].item() == 1  # the signal to the peer was still delivered
+    h3b.clear_status()
+    f0[1] = 1  # the "peer" has arrived for epoch 1
+    check(lib.h3b_peer_barrier(arr, world, 0, 1, int(5e9), _stream()), "barrier")
+    assert h3b.status() == 0
+    x = torch.ones(4, device=DEV) * 2
+    assert x.sum().item() == 8.0

@@ -1,0 +1,117 @@
+"""GPU parity of the INT8 linear path (quantiser, tcgen05 GEMM, dequant epilogue).
+
+Bar: bit-exact.  int8 activations and fp32 scales against the C oracle; int32
+accumulators against the oracle (small) and cuBLAS torch._int_mm (large);
+bf16 outputs against the oracle (small) and the same fp32 formula evaluated
+by PyTorch elementwise ops on the GPU (large).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import bits, gen, randn_bf16
+
+pytestmark = pytest.mark.gpu
+
+h3b = pytest.importorskip("h3b")
+DEV = "cuda"
+
+
+def _weights(N, K, seed):
+    g = gen(seed)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    ws = torch.rand(N, generator=g) * 9e-3 + 1e-3
+    bias = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16)
+    return w, ws, bias
+
+
+@pytest.mark.parametrize("M,K", [(37, 5120), (4096, 5120), (129, 13824), (5, 8), (64, 256)])
+def test_quant_bit_exact(M, K):
+    x = randn_bf16((M, K), seed=M * 7 + K)
+    x[0] = 0  # all-zero row: scale 0, codes 0
+    if M > 2:
+        x[2, 5] = 1e4  # one outlier dominates the row's scale
+    q_ref, s_ref = oracle.quant_rowwise(bits(x))
+    xq, xs = h3b.quant_rowwise(x.to(DEV))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(xq.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(xs.cpu().numpy().reshape(-1), s_ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (129, 264, 384), (300, 8, 128), (40, 48, 256), (256, 512, 1024)])
+def test_gemm_small_vs_oracle(M, N, K):
+    g = gen(M + N + K)
+    xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    w, ws, bias = _weights(N, K, seed=N + 1)
+    xs = torch.rand(M, 1, generator=g) * 0.05 + 1e-3
+    y_ref, acc_ref = oracle.int8_mm_scaled(xq.numpy(), w.numpy(), xs.numpy(), ws.numpy(), want_acc=True)
+    yb_ref = oracle.int8_mm_scaled(xq.numpy(), w.numpy(), xs.numpy(), ws.numpy(), bias=bits(bias))
+    xq_d, w_d, xs_d, ws_d, b_d = (t.to(DEV) for t in (xq, w, xs, ws, bias))
+    acc = h3b.int8_mm_i32(xq_d, w_d)
+    y = h3b.int8_mm_scaled(xq_d, w_d, xs_d, ws_d)
+    yb = h3b.int8_mm_scaled(xq_d, w_d, xs_d, ws_d, bias=b_d)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(acc.cpu().numpy(), acc_ref)
+    np.testing.assert_array_equal(bits(y), y_ref)
+    np.testing.assert_array_equal(bits(yb), yb_ref)
+    assert h3b.status() == 0
+
+
+@pytest.mark.parametrize("name", ["gemm_small", "gemm_bigacc"])
+def test_gemm_golden_inputs(golden_dir, name):
+    """Golden inputs/outputs of the reference kernel itself.  The fixture holds the
+    reference's fp32 epilogue values cast by truncation (Triton interpreter); the
+    GPU's int32 sums pushed through the same fp32 epilogue must truncate to the
+    fixture exactly, and the GPU's bf16 output is the nearest-even rounding of
+    those same fp32 values."""
+    d = dict(np.load(f"{golden_dir}/{name}.npz"))
+    xq, w = torch.from_numpy(d["xq"]).to(DEV), torch.from_numpy(d["w"]).to(DEV)
+    xs, ws = torch.from_numpy(d["xs"]).to(DEV), torch.from_numpy(d["ws"]).to(DEV)
+    acc = h3b.int8_mm_i32(xq, w)
+    y = h3b.int8_mm_scaled(xq, w, xs, ws)
+    torch.cuda.synchronize()
+    f = (acc.cpu().numpy().astype(np.float32) * d["xs"][:, None]) * d["ws"][None, :]
+    np.testing.assert_array_equal(oracle.f32_to_bf16(f, oracle.TRUNC), d["out"])
+    np.testing.assert_array_equal(bits(y), oracle.f32_to_bf16(f, oracle.RNE))
+    np.testing.assert_array_equal(bits(y), oracle.int8_mm_scaled(d["xq"], d["w"], d["xs"], d["ws"]))
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 5120, 5120), (1000, 15360, 5120), (777, 5120, 13824), (16000, 5120, 5120)])
+def test_gemm_large_vs_cublas(M, N, K):
+    g = gen(M ^ N ^ K)
+    xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(DEV)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(DEV)
+    xs = (torch.rand(M, 1, generator=g) * 0.05 + 1e-3).to(DEV)
+    ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(DEV)
+    bias = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    ref_acc = torch._int_mm(xq, w.t())
+    acc = h3b.int8_mm_i32(xq, w)
+    assert torch.equal(acc, ref_acc)
+    y = h3b.int8_mm_scaled(xq, w, xs, ws, bias=bias)
+    ref = ((ref_acc.float() * xs) * ws + bias.float()).to(torch.bfloat16)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    assert h3b.status() == 0
+
+
+def test_linear_config0_vs_oracle():
+    """Config 0 end to end (quant + GEMM + dequant + bias), oracle on a row sample."""
+    M, N, K = 4096, 5120, 5120
+    x = randn_bf16((M, K), seed=0)
+    w, ws, bias = _weights(N, K, seed=1)
+    y = h3b.linear(x.to(DEV), w.to(DEV), ws.to(DEV), bias.to(DEV))
+    torch.cuda.synchronize()
+    rows = np.r_[0:64, 2000:2064, M - 64:M]
+    xr = bits(x)[rows]
+    q, s = oracle.quant_rowwise(xr)
+    ref = oracle.int8_mm_scaled(q, w.numpy(), s, ws.numpy(), bias=bits(bias))
+    np.testing.assert_array_equal(bits(y)[rows], ref)
+
+
+def test_rejects_bad_shapes():
+    xq = torch.zeros(4, 100, dtype=torch.int8, device=DEV)
+    w = torch.zeros(8, 100, dtype=torch.int8, device=DEV)
+    with pytest.raises(h3b.H3BError):
+        h3b.int8_mm_i32(xq, w)  # K % 128 != 0
+    with pytest.raises(TypeError):
+        h3b.quant_rowwise(torch.zeros(4, 16, dtype=torch.bfloat16))  # CPU tensor: no CPU path
