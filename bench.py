@@ -1,0 +1,539 @@
+#!/usr/bin/env python
+"""Benchmark of the H3 DiT hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload dit_block|dit_step|linear|fused|a2a] [--seq S] [--exchange p2p|nccl]
+
+Default workload (dit_block): one synthetic DiT block of the benchmark's
+block configuration -- D=5120, 40 heads x 128, FFN 13824 (GELU-tanh), four
+INT8 linears with per-channel scales + bias, the fused adaLN norm / gate
+chain, Ulysses all-to-all around SDPA over S=128000 tokens -- split over N
+GPUs by sequence (strong scaling).  A step is one block forward over the
+rank's rows (the residual stream is restored from the step's input first).
+Timing: W untimed steps, then K steps between barrier + synchronize, CUDA
+events on the compute stream, max over ranks.  Inputs (x 1.31 GB/N, weights
+245 MB) exceed the 126 MB L2, so no flush is needed between steps.
+
+Prints ONE JSON line on rank 0.  `value` is ms per step (lower is better);
+`e2e` repeats the step through host buffers (pinned H2D of the step's input
+rows and conditioning, D2H of the output rows); `roofline` is the INT8 GEMM
+(the dominant kernel of this library) timed by CUDA events inside the timed
+region; `cpu_baseline` times the reference's eager PyTorch path on the host's
+cores on a bounded sample of the same workload (rank 0, N=1 only).
+`--impl reference` prints the CPU reference path's line instead (rank 0 only).
+The other workloads (linear = single INT8 linear of config 0, fused = the
+fused chain of config 1, a2a = the Ulysses exchange of config 2, dit_step =
+the 40-block step of config 4) are available for measurements by hand.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "minimax-h3-multi-dgx-spark_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a"], default="dit_block")
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
+    ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default=os.environ.get("H3B_EXCHANGE", "p2p"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(PEAKS_FILE) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.sel = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.sel = ["-i", uuid if uuid.startswith("GPU-") else "GPU-" + uuid]
+        except Exception:  # noqa: BLE001
+            self.sel = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", *self.sel, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            for line in out.splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 9:
+                    self.rows.append(parts)
+        return False
+
+    def summary(self):
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        smax = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+# ---------------------------------------------------------------------------
+# distributed setup
+
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("for --gpus N > 1 launch with torch.distributed.run (one process per GPU)")
+    return rank, world, local
+
+
+def init_pg(rank, world, local):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=180),
+                                device_id=dev)
+    return dev
+
+
+def max_over_ranks(v, world, dev):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(step, steps, warmup, world, dev, sample_clocks=True):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(dev) if sample_clocks else None
+    if sampler:
+        sampler.__enter__()
+        time.sleep(0.3)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.__exit__(None, None, None)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    ms = e0.elapsed_time(e1) / steps
+    return max_over_ranks(ms, world, dev), (sampler.summary() if sampler else None)
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs (seeded on CPU in row chunks, so every world size sees the same rows)
+
+ROW_CHUNK = 4128  # one latent frame of tokens
+
+
+def seeded_rows(start, stop, dim, seed, dtype=torch.bfloat16):
+    out = torch.empty(stop - start, dim, dtype=dtype)
+    c0 = start // ROW_CHUNK
+    for c in range(c0, (stop + ROW_CHUNK - 1) // ROW_CHUNK):
+        lo, hi = c * ROW_CHUNK, (c + 1) * ROW_CHUNK
+        g = torch.Generator().manual_seed(seed * 7919 + c)
+        block = torch.randn(ROW_CHUNK, dim, generator=g).to(dtype)
+        a, b = max(lo, start), min(hi, stop)
+        out[a - start:b - start] = block[a - lo:b - lo]
+    return out
+
+
+# ---------------------------------------------------------------------------
+# DiT block / step workload
+
+def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
+    import h3b
+    from h3b import model as hm
+    from h3b.trace import Trace
+
+    cfg = hm.DiTConfig(n_blocks=n_blocks, text_len=text_len)
+    dit = hm.SynthDiT(cfg, dev, seed=1)
+    peer = None
+    ctx = None
+    if world > 1:
+        if args.exchange == "p2p":
+            peer = h3b.PeerExchange(dist.group.WORLD, rank, world, seq, cfg.heads, cfg.head_dim)
+        ctx = h3b.SPContext(rank, world, dist.group.WORLD, seq, exchange=args.exchange, peer=peer)
+        h3b.startup_probe(rank, world, dist.group.WORLD, dev)
+        start, stop = ctx.start, ctx.stop
+    else:
+        start, stop = 0, seq
+    s_local = stop - start
+    x_host = seeded_rows(start, stop, cfg.dim, seed=11).pin_memory()
+    text_host = seeded_rows(0, text_len, cfg.dim, seed=12).pin_memory() if text_len else None
+    x0 = x_host.to(dev)
+    text = text_host.to(dev) if text_len else None
+    xw = torch.empty_like(x0)
+    ridx = torch.zeros(s_local, dtype=torch.int32, device=dev)
+
+    def step():
+        xw.copy_(x0)
+        dit.forward(xw, ridx, ctx, text)
+
+    ms, clocks = timed(step, args.steps, args.warmup, world, dev)
+    # per-kernel spans over a second, identical timed region (events inside it)
+    with Trace() as tr:
+        _ms2, _ = timed(step, args.steps, 0, world, dev, sample_clocks=False)
+    spans = tr.summary(args.steps)
+    launches = tr.launches / args.steps
+
+    e2e = None
+    if not args.no_e2e:
+        out_host = torch.empty_like(x_host).pin_memory()
+        e_host = [p.e.detach().cpu().pin_memory() for p in dit.params]
+
+        def step_e2e():
+            for p, eh in zip(dit.params, e_host):
+                p.e.copy_(eh, non_blocking=True)
+                p.tables = h3b.modulation_tables(*(p.e[:, i] for i in range(6)))
+            xw.copy_(x_host, non_blocking=True)
+            y = dit.forward(xw, ridx, ctx, text)
+            out_host.copy_(y, non_blocking=True)
+
+        ms_e2e, _ = timed(step_e2e, args.steps, 1, world, dev, sample_clocks=False)
+        h2d = x_host.numel() * 2 + sum(e.numel() * 2 for e in e_host)
+        e2e = {"value": round(ms_e2e, 3), "unit": "ms/step", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": out_host.numel() * 2}
+    status = h3b.status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+    if peer is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[dev.index])
+        peer.close()
+    return cfg, s_local, ms, clocks, spans, launches, e2e
+
+
+def gemm_roofline(spans, pk, src):
+    g = spans.get("gemm")
+    if not g or g["ms"] <= 0:
+        return None
+    achieved = g["work"] / (g["ms"] * 1e-3) / 1e12  # TOPS
+    peak = 2.0 * pk["bf16_tflops"]
+    return {"kernel": "gemm_i8_kernel (tcgen05 kind::i8 + dequant epilogue)", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+            "frac": round(achieved / peak, 4), "traffic": None,
+            "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TFLOP/s burst; kind::i8 issues at "
+                           "twice the kind::f16 rate on B200)",
+            "work_per_step": g["work"], "launches_per_step": g["calls"], "ms_per_step": round(g["ms"], 3)}
+
+
+def breakdown(spans, pk):
+    out = {}
+    for name, d in sorted(spans.items()):
+        item = {"ms_per_step": round(d["ms"], 3), "calls_per_step": d["calls"]}
+        if d["ms"] > 0 and d["work"] > 0:
+            if name.startswith("gemm"):
+                item["achieved_tops"] = round(d["work"] / (d["ms"] * 1e-3) / 1e12, 1)
+            elif name.startswith("a2a_fwd_p2p") or name.startswith("a2a_inv_p2p"):
+                item["off_rank_gbs"] = round(d["work"] / (d["ms"] * 1e-3) / 1e9, 1)
+            else:
+                gbs = d["work"] / (d["ms"] * 1e-3) / 1e9
+                item["achieved_gbs"] = round(gbs, 1)
+                item["hbm_frac"] = round(gbs / pk["hbm_gbs"], 3)
+        out[name] = item
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU reference path (eager PyTorch on the host cores), bounded sample
+
+class CpuReference:
+    """The reference's eager PyTorch path on the host cores, on a bounded sample.
+
+    Row-local work (norms, INT8 linears, GELU, gates) runs on `rows` rows and is
+    scaled by seq/rows; attention runs for `q_rows` query rows against all `seq`
+    keys/values of every head and is scaled by seq/q_rows.  Set-up (weights,
+    inputs) happens once; run() times one sample and returns the extrapolated
+    ms per step."""
+
+    def __init__(self, cfg, seq, rows=1024, q_rows=256):
+        from h3b import model as hm
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cfg, self.seq, self.rows, self.q_rows = cfg, seq, rows, q_rows
+        g = torch.Generator().manual_seed(5)
+        D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
+        self.p = hm.make_params(hm.DiTConfig(dim=D, heads=H, head_dim=Dh, ffn=cfg.ffn), 0, 1, torch.device("cpu"))
+        self.x = torch.randn(rows, D, generator=g).to(torch.bfloat16)
+        self.ridx = torch.zeros(rows, dtype=torch.int32)
+        self.q = torch.randn(q_rows, H, Dh, generator=g).to(torch.bfloat16)
+        self.k = torch.randn(seq, H, Dh, generator=g).to(torch.bfloat16)
+        self.v = torch.randn(seq, H, Dh, generator=g).to(torch.bfloat16)
+
+    def _rowwork(self):
+        import torch.nn.functional as F
+
+        from oracle import torch_path as tp
+        p, cfg, D = self.p, self.cfg, self.cfg.dim
+        s1a, sha, ga, s1m, shm, gm = p.tables
+        xx = self.x.clone()
+        h = tp.norm_mod(xx, p.n1w, cfg.eps, self.ridx, s1a, sha)
+        qkv = tp.linear(h, p.qkv.w, p.qkv.ws, p.qkv.b)
+        o = tp.linear(qkv[:, :D], p.out.w, p.out.ws, p.out.b)  # out-proj on an attention-output-sized input
+        h = tp.gate_norm_mod_(xx, o, ga, p.n2w, cfg.eps, self.ridx, s1m, shm)
+        u = tp.linear(h, p.up.w, p.up.ws, p.up.b)
+        m = tp.linear(F.gelu(u, approximate="tanh"), p.down.w, p.down.ws, p.down.b)
+        tp.gate_(xx, m, gm, self.ridx)
+
+    def _attn(self):
+        from oracle import torch_path as tp
+        tp.sdpa_heads(self.q, self.k, self.v)
+
+    def run(self):
+        t0 = time.perf_counter()
+        self._rowwork()
+        t_rows = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        self._attn()
+        t_attn = time.perf_counter() - t0
+        self.last_cpu_s = t_rows + t_attn
+        return (t_rows * self.seq / self.rows + t_attn * self.seq / self.q_rows) * 1e3
+
+    def sample(self):
+        return (f"eager PyTorch CPU path (oracle/torch_path.py): row-local block work (norms, 4 INT8 linears, "
+                f"GELU, gates) on {self.rows} of {self.seq} rows (x{self.seq / self.rows:.1f}) + SDPA for "
+                f"{self.q_rows} query rows vs all {self.seq} keys, {self.cfg.heads} heads "
+                f"(x{self.seq / self.q_rows:.1f}); {self.last_cpu_s:.1f} s of CPU work per sample")
+
+
+def cpu_baseline(cfg, seq, steps=3, warmup=1):
+    ref = CpuReference(cfg, seq)
+    for _ in range(warmup):
+        ref.run()
+    ms = statistics.median([ref.run() for _ in range(steps)])
+    return {"value": round(ms, 1), "unit": "ms/step", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": ref.sample()}
+
+
+# ---------------------------------------------------------------------------
+# by-hand workloads (configs 0-2)
+
+def linear_workload(args, dev):
+    import h3b
+    from h3b.trace import Trace
+    M, N, K = 4096, 5120, 5120
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(dev)
+    ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(dev)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        flush.zero_()
+        h3b.linear(x, w, ws, b)
+
+    ms, clocks = timed(step, args.steps, args.warmup, 1, dev)
+    with Trace() as tr:
+        timed(step, args.steps, 0, 1, dev, sample_clocks=False)
+    return ms, clocks, tr.summary(args.steps), tr.launches / args.steps
+
+
+def fused_workload(args, dev):
+    import h3b
+    from h3b.trace import Trace
+    S, D = 32768, 5120
+    x0 = seeded_rows(0, S, D, seed=3).to(dev)
+    o1 = seeded_rows(0, S, D, seed=4).to(dev)
+    o2 = seeded_rows(0, S, D, seed=5).to(dev)
+    g = torch.Generator().manual_seed(6)
+    e = (0.1 * torch.randn(1, 6, D, generator=g)).to(torch.bfloat16).to(dev)
+    w1 = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
+    w2 = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
+    s1a, sha, ga, s1m, shm, gm = h3b.modulation_tables(*(e[:, i] for i in range(6)))
+    ridx = torch.zeros(S, dtype=torch.int32, device=dev)
+    x = torch.empty_like(x0)
+
+    def step():
+        x.copy_(x0)
+        h3b.norm_mod(x, w1, 1e-6, ridx, s1a, sha)
+        h3b.gate_norm_mod_(x, o1, ga, w2, 1e-6, ridx, s1m, shm)
+        h3b.gate_(x, o2, gm, ridx)
+
+    ms, clocks = timed(step, args.steps, args.warmup, 1, dev)
+    with Trace() as tr:
+        timed(step, args.steps, 0, 1, dev, sample_clocks=False)
+    return ms, clocks, tr.summary(args.steps), tr.launches / args.steps
+
+
+def a2a_workload(args, rank, world, dev):
+    import h3b
+    from h3b.trace import Trace
+    S, H, Dh = args.seq or 131072, 40, 128
+    peer = h3b.PeerExchange(dist.group.WORLD, rank, world, S, H, Dh) if args.exchange == "p2p" else None
+    ctx = h3b.SPContext(rank, world, dist.group.WORLD, S, exchange=args.exchange, peer=peer)
+    q, k, v = (seeded_rows(ctx.start, ctx.stop, H * Dh, seed=20 + i).to(dev).view(-1, H, Dh) for i in range(3))
+
+    def step():
+        qq, kk, vv = h3b.a2a_gather_qkv(q, k, v, ctx)
+        h3b.a2a_scatter_seq_gather_heads(qq.reshape(S, -1), ctx)
+
+    ms, clocks = timed(step, args.steps, args.warmup, world, dev)
+    with Trace() as tr:
+        timed(step, args.steps, 0, world, dev, sample_clocks=False)
+    if peer is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[dev.index])
+        peer.close()
+    return S, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    args = parse_args()
+    rank, world, local = setup_dist(args)
+    pk, pk_src = peaks()
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from h3b import model as hm
+        seq = args.seq or 128000
+        cfg = hm.DiTConfig()
+        ref = CpuReference(cfg, seq)
+        for _ in range(args.warmup):
+            ref.run()
+        v = statistics.median([ref.run() for _ in range(args.steps)])
+        sample, cores = ref.sample(), torch.get_num_threads()
+        line = {"impl": "reference", "metric": "DiT fwd ms/step", "value": round(v, 1), "unit": "ms/step",
+                "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1),
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8+bf16",
+                "data": "synthetic (seeded N(0,1) activations, random-init int8 weights)",
+                "config": {"workload": "dit_block", "seq_len": seq, "dim": 5120, "heads": 40, "head_dim": 128,
+                           "ffn": 13824, "blocks": 1, "parallelism": "none (host CPU)"},
+                "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(v, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    dev = init_pg(rank, world, local)
+    try:
+        if args.workload in ("dit_block", "dit_step"):
+            step_cfg = args.workload == "dit_step"
+            seq = args.seq or (252000 if step_cfg else 128000)
+            n_blocks = args.blocks or (40 if step_cfg else 1)
+            text_len = 512 if step_cfg else 0
+            cfg, s_local, ms, clocks, spans, launches, e2e = dit_workload(args, rank, world, dev, n_blocks, seq,
+                                                                          text_len)
+            line = {"metric": "DiT fwd ms/step", "value": round(ms, 3), "unit": "ms/step", "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+                    "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8+bf16",
+                    "data": "synthetic (seeded N(0,1) activations, random-init int8 weights)",
+                    "config": {"workload": "dit_step" if step_cfg else "dit_block", "seq_len": seq,
+                               "local_rows": s_local, "dim": cfg.dim, "heads": cfg.heads,
+                               "head_dim": cfg.head_dim, "ffn": cfg.ffn, "blocks": n_blocks, "text_len": text_len,
+                               "parallelism": f"ulysses_sp{world}", "exchange": args.exchange if world > 1 else None,
+                               "l2": "inputs larger than L2 (no flush)"},
+                    "roofline": gemm_roofline(spans, pk, pk_src), "clocks": clocks, "e2e": e2e,
+                    "gpu_launches": int(round(launches * args.steps)), "breakdown": breakdown(spans, pk)}
+            if rank == 0 and world == 1 and not args.no_cpu_baseline and not step_cfg:
+                line["cpu_baseline"] = cpu_baseline(cfg, seq)
+        elif args.workload == "linear":
+            ms, clocks, spans, launches = linear_workload(args, dev)
+            rl = gemm_roofline(spans, pk, pk_src)
+            line = {"metric": "INT8 linear (config 0) TOPS", "value": round(2 * 4096 * 5120 * 5120 / (ms * 1e-3) / 1e12, 1),
+                    "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
+                    "config": {"workload": "linear", "M": 4096, "N": 5120, "K": 5120, "l2": "256 MB flush per step"},
+                    "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
+                    "breakdown": breakdown(spans, pk)}
+        elif args.workload == "fused":
+            ms, clocks, spans, launches = fused_workload(args, dev)
+            line = {"metric": "fused adaLN chain (config 1) ms/step", "value": round(ms, 4), "unit": "ms/step",
+                    "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+                    "dtype": "bf16", "config": {"workload": "fused", "S": 32768, "D": 5120},
+                    "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
+                    "breakdown": breakdown(spans, pk)}
+        else:
+            if world < 2:
+                raise SystemExit("the a2a workload needs --gpus >= 2")
+            S, ms, clocks, spans, launches = a2a_workload(args, rank, world, dev)
+            buf = S // world * 40 * 128 * 2
+            bus = 4 * buf * (world - 1) / world / (ms * 1e-3) / 1e9
+            line = {"metric": "Ulysses a2a bus GB/s (q,k,v forward + inverse)", "value": round(bus, 1),
+                    "unit": "GB/s", "ms_per_step": round(ms, 4), "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
+                    "config": {"workload": "a2a", "S": S, "heads": 40, "head_dim": 128, "exchange": args.exchange},
+                    "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
+                    "breakdown": breakdown(spans, pk)}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

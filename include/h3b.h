@@ -117,12 +117,13 @@ H3B_API int h3b_gate_(void *x, const void *o, const void *g, const int32_t *ridx
 
 /* ---- Ulysses all-to-all -------------------------------------------------- */
 
-/* Forward pack: t [s_local, P * chunk] -> send [P, s_local, chunk]
- * (chunk = (H/P)*Dh elements, given in bytes).  The NCCL exchange that
- * follows receives [S, chunk] already in sequence order.
+/* Forward pack: t [s_local, P * chunk] (row stride t_ld bytes) -> send
+ * [P, s_local, chunk] (chunk = (H/P)*Dh elements, given in bytes).  The NCCL
+ * exchange that follows receives [S, chunk] already in sequence order.
  * Replaces t.reshape(s_local, p, chunk).transpose(0, 1).contiguous() of
  * comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:185. */
-H3B_API int h3b_a2a_pack(const void *t, void *send, int64_t s_local, int64_t chunk_bytes, int world, void *stream);
+H3B_API int h3b_a2a_pack(const void *t, int64_t t_ld, void *send, int64_t s_local, int64_t chunk_bytes, int world,
+                         void *stream);
 
 /* Inverse unpack: recv [P, s_local, chunk] -> out [s_local, P * chunk].
  * Replaces out.view(p, s_local, chunk).transpose(0, 1).reshape(...) of
@@ -149,12 +150,13 @@ H3B_API int h3b_peer_barrier(uint32_t *const *peer_flags, int world, int rank, u
                      void *stream);
 
 /* Forward exchange fused with the pack, over peer memory: for each of n
- * tensors src[i] [s_local, P * chunk] and each rank j, rows go straight into
- * rank j's receive buffer dst[i * P + j] ([S, chunk]) at rows
- * row_start .. row_start + s_local.  Bracket with h3b_peer_barrier.
+ * tensors src[i] [s_local, P * chunk] (row stride src_ld bytes, shared by all
+ * n) and each rank j, rows go straight into rank j's receive buffer
+ * dst[i * P + j] ([S, chunk]) at rows row_start .. row_start + s_local.
+ * Bracket with h3b_peer_barrier.
  * Replaces a2a_gather_seq_scatter_heads / _seq_gather, sp_forward.py:158-166,179-188. */
-H3B_API int h3b_a2a_fwd_p2p(int n, const void *const *src, void *const *dst, int64_t s_local, int64_t row_start,
-                    int64_t chunk_bytes, int world, void *stream);
+H3B_API int h3b_a2a_fwd_p2p(int n, const void *const *src, int64_t src_ld, void *const *dst, int64_t s_local,
+                            int64_t row_start, int64_t chunk_bytes, int world, void *stream);
 
 /* Inverse exchange fused with the unpack: src [S, chunk] rows (leading
  * dimension src_ld bytes) split by `splits` (P entries) go to rank j's

@@ -16,10 +16,10 @@ constexpr int kMaxWorld = 8;
 constexpr int kMaxFwdTensors = 4;
 
 // One CTA per source row s; vector e of the row goes to block j = e / cv.
-__global__ void __launch_bounds__(256) pack_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
-                                                   int64_t s_local, int cv, int world) {
+__global__ void __launch_bounds__(256) pack_kernel(const uint4* __restrict__ src, int64_t src_ldv,
+                                                   uint4* __restrict__ dst, int64_t s_local, int cv, int world) {
     for (int64_t s = blockIdx.x; s < s_local; s += gridDim.x) {
-        const uint4* row = src + s * (int64_t)cv * world;
+        const uint4* row = src + s * src_ldv;
         for (int e = threadIdx.x; e < cv * world; e += blockDim.x) {
             const int j = e / cv, v = e - j * cv;
             dst[((int64_t)j * s_local + s) * cv + v] = row[e];
@@ -44,12 +44,12 @@ struct FwdP2PArgs {
 };
 
 // blockIdx.y = tensor.  dst[i][j] row (row_start + s) <- src[i] row s block j.
-__global__ void __launch_bounds__(256) fwd_p2p_kernel(FwdP2PArgs a, int64_t s_local, int64_t row_start, int cv,
-                                                      int world) {
+__global__ void __launch_bounds__(256) fwd_p2p_kernel(FwdP2PArgs a, int64_t src_ldv, int64_t s_local,
+                                                      int64_t row_start, int cv, int world) {
     const int i = blockIdx.y;
     const uint4* src = a.src[i];
     for (int64_t s = blockIdx.x; s < s_local; s += gridDim.x) {
-        const uint4* row = src + s * (int64_t)cv * world;
+        const uint4* row = src + s * src_ldv;
         for (int e = threadIdx.x; e < cv * world; e += blockDim.x) {
             const int j = e / cv, v = e - j * cv;
             a.dst[i][j][(row_start + s) * cv + v] = row[e];
@@ -120,15 +120,16 @@ static unsigned copy_grid(int64_t rows) {
 
 using namespace h3b;
 
-extern "C" int h3b_a2a_pack(const void* t, void* send, int64_t s_local, int64_t chunk_bytes, int world,
-                            void* stream) {
+extern "C" int h3b_a2a_pack(const void* t, int64_t t_ld, void* send, int64_t s_local, int64_t chunk_bytes,
+                            int world, void* stream) {
     H3B_REQUIRE(t && send, "h3b_a2a_pack: NULL pointer");
+    H3B_REQUIRE(t_ld >= chunk_bytes * world && t_ld % 16 == 0, "h3b_a2a_pack: t_ld=%lld must be >= a row and a multiple of 16", (long long)t_ld);
     H3B_REQUIRE(world >= 1 && s_local >= 0 && chunk_bytes > 0 && chunk_bytes % 16 == 0 && chunk_bytes * world < (1ll << 31),
                 "h3b_a2a_pack: chunk_bytes=%lld must be a positive multiple of 16", (long long)chunk_bytes);
     H3B_REQUIRE(aligned(t, 16) && aligned(send, 16), "h3b_a2a_pack: buffers must be 16-byte aligned");
     if (s_local == 0) return H3B_OK;
     pack_kernel<<<copy_grid(s_local), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint4*>(t), static_cast<uint4*>(send), s_local, (int)(chunk_bytes / 16), world);
+        static_cast<const uint4*>(t), t_ld / 16, static_cast<uint4*>(send), s_local, (int)(chunk_bytes / 16), world);
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
 }
@@ -163,12 +164,13 @@ extern "C" int h3b_peer_barrier(uint32_t* const* peer_flags, int world, int rank
     return H3B_OK;
 }
 
-extern "C" int h3b_a2a_fwd_p2p(int n, const void* const* src, void* const* dst, int64_t s_local, int64_t row_start,
-                               int64_t chunk_bytes, int world, void* stream) {
+extern "C" int h3b_a2a_fwd_p2p(int n, const void* const* src, int64_t src_ld, void* const* dst, int64_t s_local,
+                               int64_t row_start, int64_t chunk_bytes, int world, void* stream) {
     H3B_REQUIRE(n >= 1 && n <= kMaxFwdTensors && src && dst, "h3b_a2a_fwd_p2p: bad tensor count %d", n);
     H3B_REQUIRE(world >= 1 && world <= kMaxWorld, "h3b_a2a_fwd_p2p: world=%d out of range", world);
     H3B_REQUIRE(s_local >= 0 && row_start >= 0 && chunk_bytes > 0 && chunk_bytes % 16 == 0 && chunk_bytes * world < (1ll << 31),
                 "h3b_a2a_fwd_p2p: chunk_bytes=%lld must be a positive multiple of 16", (long long)chunk_bytes);
+    H3B_REQUIRE(src_ld >= chunk_bytes * world && src_ld % 16 == 0, "h3b_a2a_fwd_p2p: src_ld=%lld must be >= a row and a multiple of 16", (long long)src_ld);
     FwdP2PArgs a{};
     for (int i = 0; i < n; ++i) {
         H3B_REQUIRE(src[i] && aligned(src[i], 16), "h3b_a2a_fwd_p2p: src[%d] NULL/misaligned", i);
@@ -180,7 +182,8 @@ extern "C" int h3b_a2a_fwd_p2p(int n, const void* const* src, void* const* dst, 
     }
     if (s_local == 0) return H3B_OK;
     dim3 grid(copy_grid(s_local), n);
-    fwd_p2p_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, s_local, row_start, (int)(chunk_bytes / 16), world);
+    fwd_p2p_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, src_ld / 16, s_local, row_start,
+                                                                         (int)(chunk_bytes / 16), world);
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
 }

@@ -11,6 +11,7 @@ plus the per-forward helpers of comfyui_nodes/h3-fuse-graph/h3_fuse_patch.py:
 import torch
 
 from ._lib import check, lib, ptr, require_cuda, stream_of
+from .trace import span
 
 BF16 = torch.bfloat16
 
@@ -36,8 +37,9 @@ def norm_mod(x, w, eps, ridx, s1, sh):
     """h = bf16(rbf16(rbf16(w * (rstd * x)) * s1[r]) + sh[r]) per row (x bf16 [S,D])."""
     S, D, R = _check(x, w, ridx, s1, sh)
     h = torch.empty_like(x)
-    check(lib.h3b_norm_mod(ptr(x), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh), ptr(h), S, D, R, stream_of(x)),
-          "h3b_norm_mod")
+    with span("norm_mod", 4 * S * D):
+        check(lib.h3b_norm_mod(ptr(x), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh), ptr(h), S, D, R, stream_of(x)),
+              "h3b_norm_mod")
     return h
 
 
@@ -50,8 +52,9 @@ def gate_norm_mod_(x, o, g, w, eps, ridx, s1, sh):
     if g.dtype != BF16 or tuple(g.shape) != (R, D) or not g.is_contiguous():
         raise ValueError("gate_norm_mod_: g must be a contiguous bf16 [R, D] table")
     h = torch.empty_like(x)
-    check(lib.h3b_gate_norm_mod_(ptr(x), ptr(o), ptr(g), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh), ptr(h),
-                                 S, D, R, stream_of(x)), "h3b_gate_norm_mod_")
+    with span("gate_norm_mod_", 8 * S * D):
+        check(lib.h3b_gate_norm_mod_(ptr(x), ptr(o), ptr(g), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh), ptr(h),
+                                     S, D, R, stream_of(x)), "h3b_gate_norm_mod_")
     return h
 
 
@@ -67,7 +70,8 @@ def gate_(x, o, g, ridx):
         raise ValueError("gate_: g must be a contiguous bf16 [R, D] table")
     if ridx.dtype != torch.int32 or ridx.numel() != S:
         raise ValueError("gate_: ridx must be int32 [S]")
-    check(lib.h3b_gate_(ptr(x), ptr(o), ptr(g), ptr(ridx), S, D, g.shape[0], stream_of(x)), "h3b_gate_")
+    with span("gate_", 6 * S * D):
+        check(lib.h3b_gate_(ptr(x), ptr(o), ptr(g), ptr(ridx), S, D, g.shape[0], stream_of(x)), "h3b_gate_")
     return x
 
 

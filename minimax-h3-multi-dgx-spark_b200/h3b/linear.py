@@ -11,6 +11,7 @@ kernels run on the current CUDA stream, shape/dtype violations raise.
 import torch
 
 from ._lib import check, lib, ptr, require_cuda, stream_of
+from .trace import span
 
 
 def supported(K):
@@ -31,7 +32,8 @@ def quant_rowwise(x, xq=None, xs=None):
         xq = torch.empty((M, K), dtype=torch.int8, device=x.device)
     if xs is None:
         xs = torch.empty((M, 1), dtype=torch.float32, device=x.device)
-    check(lib.h3b_quant_rowwise(ptr(x), x.stride(0), M, K, ptr(xq), ptr(xs), stream_of(x)), "h3b_quant_rowwise")
+    with span("quant", 3 * M * K + 4 * M):
+        check(lib.h3b_quant_rowwise(ptr(x), x.stride(0), M, K, ptr(xq), ptr(xs), stream_of(x)), "h3b_quant_rowwise")
     return xq, xs
 
 
@@ -60,8 +62,9 @@ def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
         bias = bias.contiguous()
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
-    check(lib.h3b_int8_mm_scaled(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
-          "h3b_int8_mm_scaled")
+    with span("gemm", 2 * M * N * K):
+        check(lib.h3b_int8_mm_scaled(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
+              "h3b_int8_mm_scaled")
     return out
 
 
@@ -70,7 +73,8 @@ def int8_mm_i32(xq, w, out=None):
     M, N, K = _gemm_checks(xq, w)
     if out is None:
         out = torch.empty((M, N), dtype=torch.int32, device=xq.device)
-    check(lib.h3b_int8_mm_i32(ptr(xq), ptr(w), ptr(out), M, N, K, stream_of(xq)), "h3b_int8_mm_i32")
+    with span("gemm_i32", 2 * M * N * K):
+        check(lib.h3b_int8_mm_i32(ptr(xq), ptr(w), ptr(out), M, N, K, stream_of(xq)), "h3b_int8_mm_i32")
     return out
 
 

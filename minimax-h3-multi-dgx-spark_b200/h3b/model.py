@@ -1,0 +1,167 @@
+"""Synthetic H3-style DiT block/step driving the hot path (the benchmark caller).
+
+ComfyUI's MiniMax H3 model is not part of this project, so the benchmark
+configurations use a random-init stand-in with the same block structure:
+
+  fused DiTBlock.forward   comfyui_nodes/h3-fuse-graph/h3_fuse_patch.py:96-143
+      h = norm_mod(x, w1, eps, ridx, s1a, sha)
+      o = attention(h)                      sp_attention, sp_forward.py:276-318
+      h = gate_norm_mod_(x, o, ga, w2, eps, ridx, s1m, shm)
+      o = mlp(h)                            up INT8 linear -> GELU(tanh) -> down INT8 linear
+      gate_(x, o, gm, ridx)
+  sp_attention: qkv INT8 linear -> Ulysses forward all-to-all (q, k, v) ->
+      SDPA over [1, H/P, S, Dh] -> inverse all-to-all -> out INT8 linear.
+
+Optional text cross-attention (the 40-block step configuration): a second,
+row-local attention branch from the same modulated h to a replicated text
+context (q / kv / out INT8 linears); its output is added to the self-attention
+output before the gated residual, so the fused norm chain is unchanged and no
+exchange is needed for it.  The reference model has no such branch in this
+file set; the layout is this harness's choice.
+
+Weights are int8 with per-output-channel fp32 scales and bf16 biases, drawn
+from a seeded generator on the target device.  Attention stays PyTorch's
+scaled_dot_product_attention, as in the reference.
+"""
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import fuse, linear, sp
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class Linear8:
+    w: torch.Tensor  # int8 [N, K]
+    ws: torch.Tensor  # fp32 [N]
+    b: torch.Tensor  # bf16 [N]
+
+    @staticmethod
+    def random(n, k, gen, device):
+        w = torch.randint(-127, 128, (n, k), generator=gen, device=device, dtype=torch.int8)
+        # per-channel scales sized so a unit-variance input gives an O(1) output
+        ws = (torch.rand(n, generator=gen, device=device) + 0.5) / (127.0 * k ** 0.5)
+        b = (torch.randn(n, generator=gen, device=device) * 0.02).to(BF16)
+        return Linear8(w, ws, b)
+
+
+@dataclass
+class BlockParams:
+    n1w: torch.Tensor
+    n2w: torch.Tensor
+    qkv: Linear8
+    out: Linear8
+    up: Linear8
+    down: Linear8
+    e: torch.Tensor  # bf16 [R, 6, D] adaLN conditioning (shift/scale/gate x 2)
+    cq: Linear8 = None
+    ckv: Linear8 = None
+    cout: Linear8 = None
+    tables: tuple = field(default=None, repr=False)
+
+
+@dataclass
+class DiTConfig:
+    dim: int = 5120
+    heads: int = 40
+    head_dim: int = 128
+    ffn: int = 13824
+    eps: float = 1e-6
+    n_blocks: int = 1
+    text_len: int = 0  # > 0 enables the cross-attention branch
+
+
+def make_params(cfg, block_index, seed, device, R=1):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000003 + block_index)
+    D = cfg.dim
+    p = BlockParams(
+        n1w=(1 + 0.02 * torch.randn(D, generator=g, device=device)).to(BF16),
+        n2w=(1 + 0.02 * torch.randn(D, generator=g, device=device)).to(BF16),
+        qkv=Linear8.random(3 * D, D, g, device),
+        out=Linear8.random(D, D, g, device),
+        up=Linear8.random(cfg.ffn, D, g, device),
+        down=Linear8.random(D, cfg.ffn, g, device),
+        e=(0.1 * torch.randn(R, 6, D, generator=g, device=device)).to(BF16),
+    )
+    if cfg.text_len:
+        p.cq = Linear8.random(D, D, g, device)
+        p.ckv = Linear8.random(2 * D, D, g, device)
+        p.cout = Linear8.random(D, D, g, device)
+    p.tables = fuse.modulation_tables(*(p.e[:, i] for i in range(6)))
+    return p
+
+
+def _lin(x, l):
+    return linear.linear(x, l.w, l.ws, l.b)
+
+
+def sdpa_heads(q, k, v):
+    """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h*Dh] via SDPA on [1, h, S, Dh] views."""
+    o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
+                                       v.transpose(0, 1).unsqueeze(0))
+    sq, h, dh = q.shape
+    return o.squeeze(0).transpose(0, 1).reshape(sq, h * dh)
+
+
+def self_attention(cfg, p, h, ctx):
+    s = h.shape[0]
+    D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
+    qkv = _lin(h, p.qkv)  # [s, 3D]
+    q = qkv[:, :D].view(s, H, Dh)
+    k = qkv[:, D:2 * D].view(s, H, Dh)
+    v = qkv[:, 2 * D:].view(s, H, Dh)
+    if ctx is None or ctx.world == 1:
+        return _lin(sdpa_heads(q, k, v), p.out)
+    q, k, v = sp.a2a_gather_qkv(q, k, v, ctx)  # [S, H/P, Dh] each
+    o = sdpa_heads(q, k, v)  # [S, (H/P)*Dh]
+    o = sp.a2a_scatter_seq_gather_heads(o, ctx)  # [s_local, D]
+    return _lin(o, p.out)
+
+
+def cross_attention(cfg, p, h, text):
+    s = h.shape[0]
+    D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
+    q = _lin(h, p.cq).view(s, H, Dh)
+    kv = _lin(text, p.ckv)
+    t = text.shape[0]
+    k = kv[:, :D].view(t, H, Dh)
+    v = kv[:, D:].view(t, H, Dh)
+    return _lin(sdpa_heads(q, k, v), p.cout)
+
+
+def block_forward(cfg, p, x, ridx, ctx=None, text=None):
+    """One fused DiT block on the rank's rows x [s_local, D] (updated in place and returned)."""
+    s1a, sha, ga, s1m, shm, gm = p.tables
+    h = fuse.norm_mod(x, p.n1w, cfg.eps, ridx, s1a, sha)
+    o = self_attention(cfg, p, h, ctx)
+    if text is not None:
+        o = o + cross_attention(cfg, p, h, text)
+    del h
+    h = fuse.gate_norm_mod_(x, o, ga, p.n2w, cfg.eps, ridx, s1m, shm)
+    del o
+    u = _lin(h, p.up)
+    del h
+    a = F.gelu(u, approximate="tanh")
+    del u
+    m = _lin(a, p.down)
+    del a
+    fuse.gate_(x, m, gm, ridx)
+    return x
+
+
+class SynthDiT:
+    """n_blocks random-init blocks; forward runs them in order on the rank's rows."""
+
+    def __init__(self, cfg, device, seed=0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.params = [make_params(cfg, i, seed, self.device) for i in range(cfg.n_blocks)]
+
+    def forward(self, x, ridx, ctx=None, text=None):
+        for p in self.params:
+            x = block_forward(self.cfg, p, x, ridx, ctx, text)
+        return x

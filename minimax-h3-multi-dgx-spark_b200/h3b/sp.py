@@ -25,6 +25,7 @@ import torch
 import torch.distributed as dist
 
 from ._lib import check, lib, ptr, ptr_array, require_cuda, stream_of
+from .trace import span
 
 
 class SPContext:
@@ -68,18 +69,26 @@ def _seq_scatter(out, send, ctx, width, async_op=False):
                                   group=ctx.group, async_op=async_op)
 
 
+def _rows(t):
+    """View t as [rows, row_elems] with unit element stride inside a row; returns (t2d, row stride)."""
+    t2 = t.reshape(t.shape[0], -1) if t.dim() != 2 else t
+    if t2.stride(-1) != 1:
+        t2 = t2.contiguous()
+    return t2, t2.stride(0)
+
+
 def pack(t, world):
-    """[s_local, P*chunk] (any trailing shape) -> [P, s_local, chunk] with the pack kernel."""
+    """[s_local, P*chunk] (rows may be strided) -> [P, s_local, chunk] with the pack kernel."""
     require_cuda(t)
-    s_local = t.shape[0]
-    row_elems = t[0].numel() if s_local else t.numel()
+    t2, ld = _rows(t)
+    s_local, row_elems = t2.shape
     if row_elems % world:
         raise ValueError("pack: the row does not split into world chunks")
     chunk = row_elems // world
-    t = t.contiguous()
     send = torch.empty((world, s_local, chunk), dtype=t.dtype, device=t.device)
-    check(lib.h3b_a2a_pack(ptr(t), ptr(send), s_local, chunk * t.element_size(), world, stream_of(t)),
-          "h3b_a2a_pack")
+    es = t.element_size()
+    with span("a2a_pack", 2 * s_local * row_elems * es):
+        check(lib.h3b_a2a_pack(ptr(t2), ld * es, ptr(send), s_local, chunk * es, world, stream_of(t)), "h3b_a2a_pack")
     return send
 
 
@@ -89,8 +98,9 @@ def unpack(recv):
     world, s_local, chunk = recv.shape
     recv = recv.contiguous()
     out = torch.empty((s_local, world * chunk), dtype=recv.dtype, device=recv.device)
-    check(lib.h3b_a2a_unpack(ptr(recv), ptr(out), s_local, chunk * recv.element_size(), world, stream_of(recv)),
-          "h3b_a2a_unpack")
+    with span("a2a_unpack", 2 * recv.numel() * recv.element_size()):
+        check(lib.h3b_a2a_unpack(ptr(recv), ptr(out), s_local, chunk * recv.element_size(), world, stream_of(recv)),
+              "h3b_a2a_unpack")
     return out
 
 
@@ -100,7 +110,7 @@ def a2a_gather_seq_scatter_heads(t, ctx):
     hp = heads // ctx.world
     if ctx.exchange == "p2p":
         return ctx.peer.fwd([t], ctx)[0]
-    send = pack(t.reshape(s_local, heads * dim), ctx.world).view(-1)
+    send = pack(t, ctx.world).view(-1)
     out = torch.empty(ctx.seq_len * hp * dim, dtype=t.dtype, device=t.device)
     _seq_gather(out, send, ctx, hp * dim)
     return out.view(ctx.seq_len, hp, dim)
@@ -115,7 +125,7 @@ def a2a_gather_qkv(q, k, v, ctx):
     hp = heads // ctx.world
     outs, reqs = [], []
     for t in (q, k, v):
-        send = pack(t.reshape(s_local, heads * dim), ctx.world).view(-1)
+        send = pack(t, ctx.world).view(-1)
         out = torch.empty(ctx.seq_len * hp * dim, dtype=t.dtype, device=t.device)
         reqs.append((_seq_gather(out, send, ctx, hp * dim, async_op=True), send))
         outs.append(out.view(ctx.seq_len, hp, dim))
@@ -201,8 +211,9 @@ class PeerExchange:
     def barrier(self, stream_tensor):
         self.epoch += 1
         arr, keep = ptr_array(self.peer_flags)
-        check(lib.h3b_peer_barrier(arr, self.world, self.rank, self.epoch, self.timeout_ns, stream_of(stream_tensor)),
-              "h3b_peer_barrier")
+        with span("peer_barrier", 0):
+            check(lib.h3b_peer_barrier(arr, self.world, self.rank, self.epoch, self.timeout_ns,
+                                       stream_of(stream_tensor)), "h3b_peer_barrier")
         del keep
 
     def fwd(self, tensors, ctx):
@@ -213,16 +224,24 @@ class PeerExchange:
         s_local, heads, dim = tensors[0].shape
         if heads != self.heads or dim != self.head_dim or ctx.seq_len > self.seq_len:
             raise ValueError("tensor shape does not match the PeerExchange buffers")
-        srcs = [t.contiguous() for t in tensors]
+        srcs = [_rows(t) for t in tensors]
+        ld = srcs[0][1]
+        if any(s[1] != ld for s in srcs):
+            srcs = [(t.contiguous(), t[0].numel()) for t, _ in srcs]
+            ld = srcs[0][1]
+        srcs = [t for t, _ in srcs]
         for t in srcs:
             require_cuda(t)
             if t.dtype != self.dtype or t.shape != srcs[0].shape:
                 raise ValueError("all tensors must share shape and dtype")
+        es = srcs[0].element_size()
         src_arr, k1 = ptr_array([t.data_ptr() for t in srcs])
         dst_arr, k2 = ptr_array([self.peer_recv[i][j] for i in range(n) for j in range(self.world)])
         self.barrier(srcs[0])
-        check(lib.h3b_a2a_fwd_p2p(n, src_arr, dst_arr, s_local, ctx.start, self.chunk * srcs[0].element_size(),
-                                  self.world, stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
+        off_rank = n * s_local * self.chunk * es * (self.world - 1)
+        with span("a2a_fwd_p2p", off_rank):
+            check(lib.h3b_a2a_fwd_p2p(n, src_arr, ld * es, dst_arr, s_local, ctx.start, self.chunk * es, self.world,
+                                      stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
         self.barrier(srcs[0])
         del k1, k2
         hp = heads // self.world
@@ -236,9 +255,11 @@ class PeerExchange:
         dst_arr, k1 = ptr_array(self.peer_out)
         splits = (ctypes.c_int64 * self.world)(*ctx.splits)
         self.barrier(t)
-        check(lib.h3b_a2a_inv_p2p(ptr(t), t.stride(0) * t.element_size(), dst_arr, splits,
-                                  self.chunk * t.element_size(), self.world, self.rank, stream_of(t)),
-              "h3b_a2a_inv_p2p")
+        off_rank = (ctx.seq_len - ctx.local) * self.chunk * t.element_size()
+        with span("a2a_inv_p2p", off_rank):
+            check(lib.h3b_a2a_inv_p2p(ptr(t), t.stride(0) * t.element_size(), dst_arr, splits,
+                                      self.chunk * t.element_size(), self.world, self.rank, stream_of(t)),
+                  "h3b_a2a_inv_p2p")
         self.barrier(t)
         del k1
         return self.out[: ctx.local]

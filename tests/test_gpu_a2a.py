@@ -36,6 +36,16 @@ def test_pack_unpack(world, s_local):
     np.testing.assert_array_equal(bits(back), bits(t).reshape(s_local, H * DH))
 
 
+def test_pack_strided_rows():
+    """q of a fused qkv output: rows with stride 3*H*Dh are packed without a copy."""
+    world, s_local = 4, 300
+    qkv = randn_bf16((s_local, 3 * H * DH), seed=77)
+    q = qkv.to(DEV)[:, H * DH:2 * H * DH]  # the k third, strided rows
+    send = h3b.pack(q, world)
+    ref = sp_layout.pack_fwd(bits(qkv)[:, H * DH:2 * H * DH].reshape(s_local, H, DH), world)
+    np.testing.assert_array_equal(bits(send), ref)
+
+
 def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -56,7 +66,8 @@ def test_p2p_kernels_emulated(world, S):
     for r in range(world):
         src, k1 = ptr_array([qd[r].data_ptr(), kd[r].data_ptr()])
         dst, k2 = ptr_array([t.data_ptr() for t in recv_q] + [t.data_ptr() for t in recv_k])
-        check(lib.h3b_a2a_fwd_p2p(2, src, dst, splits[r], starts[r], chunk * 2, world, _stream()), "fwd_p2p")
+        check(lib.h3b_a2a_fwd_p2p(2, src, H * DH * 2, dst, splits[r], starts[r], chunk * 2, world, _stream()),
+              "fwd_p2p")
     torch.cuda.synchronize()
     ref_q = sp_layout.a2a_fwd([bits(q) for q in qs], world)
     ref_k = sp_layout.a2a_fwd([bits(k) for k in ks], world)
