@@ -28,7 +28,8 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
-from . import fuse, linear, sp
+from . import fuse, sp
+from .linear import linear as _linear8
 
 BF16 = torch.bfloat16
 
@@ -96,7 +97,7 @@ def make_params(cfg, block_index, seed, device, R=1):
 
 
 def _lin(x, l):
-    return linear.linear(x, l.w, l.ws, l.b)
+    return _linear8(x, l.w, l.ws, l.b)
 
 
 def sdpa_heads(q, k, v):
