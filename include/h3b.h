@@ -91,6 +91,19 @@ H3B_API int h3b_int8_mm_i32(const int8_t *xq, const int8_t *w, int32_t *acc, int
 H3B_API int h3b_int8_linear(const void *x, int64_t M, int64_t K, const int8_t *w, const float *ws, const void *bias,
                     int64_t N, void *out, int8_t *xq_scratch, float *xs_scratch, void *stream);
 
+/* h3b_int8_linear without caller-provided scratch, for callers that cannot
+ * allocate device memory (a C/FFI host with no device allocator of its own,
+ * or a serving loop that must not call cudaMalloc mid-step).  The int8 codes
+ * and row scales go to fixed device arrays inside the library: M * K <= 8 MiB
+ * and M <= 65536, larger calls are rejected with H3B_ERR_ARG.  Each GPU that
+ * loads the library holds those 8.25 MiB until exit.  The first call on a
+ * device looks up the arrays' device addresses (make it before any stream
+ * capture).  Calls share the arrays: calls that overlap on the GPU race.
+ * No counterpart in the reference (it always allocates x_q / x_s,
+ * h3_linear_fast_patch.py:90-91); allocates nothing itself. */
+H3B_API int h3b_int8_linear_noalloc(const void *x, int64_t M, int64_t K, const int8_t *w, const float *ws,
+                                    const void *bias, int64_t N, void *out, void *stream);
+
 /* ---- fused RMSNorm / adaLN modulation / gate / residual ----------------- */
 /* x, o, h bf16 [S,D]; w bf16 [D]; ridx int32 [S] selects a row of the bf16
  * modulation tables s1 / sh / g [R,D] (0 <= ridx < R is checked on the

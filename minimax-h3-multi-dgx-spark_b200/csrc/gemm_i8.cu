@@ -484,3 +484,68 @@ extern "C" int h3b_int8_linear(const void* x, int64_t M, int64_t K, const int8_t
     if (int rc = quant_rowwise(x, K, M, K, xq_scratch, xs_scratch, s)) return rc;
     return h3b_int8_mm_scaled(xq_scratch, w, xs_scratch, ws, bias, out, M, N, K, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free INT8 linear.  Some callers cannot allocate device memory for
+// the quantised activations: a C or FFI host that binds this library without
+// a device allocator of its own, or a serving loop that must not call
+// cudaMalloc (which synchronises the device) in the middle of a step.  For
+// them the activation codes and per-row scales live in fixed file-scope
+// device arrays.  Every GPU that loads the library holds these arrays
+// (8 MiB + 256 KiB) until the process exits; calls beyond their size are
+// rejected.  All calls share the arrays, so calls that overlap on the GPU
+// (two streams, or two threads) race; the quantiser rewrites every code and
+// scale a call reads, so nothing needs clearing between calls.
+
+namespace h3b {
+namespace noalloc {
+
+constexpr int64_t kCodesBytes = 8ll << 20;  // M * K int8 activation codes
+constexpr int64_t kMaxRows = 65536;         // M fp32 per-row scales
+
+static __device__ __align__(256) int8_t g_codes[kCodesBytes];
+static __device__ __align__(256) float g_scales[kMaxRows];
+
+struct Scratch {
+    int8_t* codes;
+    float* scales;
+};
+
+// The host-side names g_codes / g_scales are stand-ins, not device addresses:
+// the device addresses are looked up once per device, with that device
+// current, on the first call made on it.
+static int scratch_for_current_device(Scratch* out) {
+    constexpr int kMaxDevices = 64;
+    static Scratch cache[kMaxDevices] = {};
+    int dev = 0;
+    H3B_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_error(H3B_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    if (!cache[dev].codes) {
+        void* c = nullptr;
+        void* s = nullptr;
+        H3B_CUDA_TRY(cudaGetSymbolAddress(&c, g_codes));
+        H3B_CUDA_TRY(cudaGetSymbolAddress(&s, g_scales));
+        cache[dev].scales = static_cast<float*>(s);
+        cache[dev].codes = static_cast<int8_t*>(c);
+    }
+    *out = cache[dev];
+    return H3B_OK;
+}
+
+}  // namespace noalloc
+}  // namespace h3b
+
+extern "C" int h3b_int8_linear_noalloc(const void* x, int64_t M, int64_t K, const int8_t* w, const float* ws,
+                                       const void* bias, int64_t N, void* out, void* stream) {
+    H3B_REQUIRE(M >= 0 && K > 0 && K % gemm::BK == 0, "h3b_int8_linear_noalloc: K=%lld must be a positive multiple of %d",
+                (long long)K, gemm::BK);
+    H3B_REQUIRE(M <= noalloc::kMaxRows,
+                "h3b_int8_linear_noalloc: M=%lld rows exceed the built-in scale buffer (%lld rows); use h3b_int8_linear",
+                (long long)M, (long long)noalloc::kMaxRows);
+    H3B_REQUIRE(M * K <= noalloc::kCodesBytes,
+                "h3b_int8_linear_noalloc: M*K=%lld exceeds the built-in %lld-byte activation buffer; use h3b_int8_linear",
+                (long long)(M * K), (long long)noalloc::kCodesBytes);
+    noalloc::Scratch sc;
+    if (int rc = noalloc::scratch_for_current_device(&sc)) return rc;
+    return h3b_int8_linear(x, M, K, w, ws, bias, N, out, sc.codes, sc.scales, stream);
+}
