@@ -59,6 +59,7 @@ def parse_args():
     ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a"], default="dit_block")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
     ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
+    ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / S of the fused workload")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default=os.environ.get("H3B_EXCHANGE", "p2p"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -381,7 +382,7 @@ def cpu_baseline(cfg, seq, steps=3, warmup=1):
 def linear_workload(args, dev):
     import h3b
     from h3b.trace import Trace
-    M, N, K = 4096, 5120, 5120
+    M, N, K = args.rows or 4096, 5120, 5120
     g = torch.Generator().manual_seed(0)
     x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
     w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(dev)
@@ -402,7 +403,7 @@ def linear_workload(args, dev):
 def fused_workload(args, dev):
     import h3b
     from h3b.trace import Trace
-    S, D = 32768, 5120
+    S, D = args.rows or 32768, 5120
     x0 = seeded_rows(0, S, D, seed=3).to(dev)
     o1 = seeded_rows(0, S, D, seed=4).to(dev)
     o2 = seeded_rows(0, S, D, seed=5).to(dev)
@@ -503,17 +504,18 @@ def main():
         elif args.workload == "linear":
             ms, clocks, spans, launches = linear_workload(args, dev)
             rl = gemm_roofline(spans, pk, pk_src)
-            line = {"metric": "INT8 linear (config 0) TOPS", "value": round(2 * 4096 * 5120 * 5120 / (ms * 1e-3) / 1e12, 1),
+            M = args.rows or 4096
+            line = {"metric": "INT8 linear (config 0) TOPS", "value": round(2 * M * 5120 * 5120 / (ms * 1e-3) / 1e12, 1),
                     "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
-                    "config": {"workload": "linear", "M": 4096, "N": 5120, "K": 5120, "l2": "256 MB flush per step"},
+                    "config": {"workload": "linear", "M": M, "N": 5120, "K": 5120, "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
         elif args.workload == "fused":
             ms, clocks, spans, launches = fused_workload(args, dev)
             line = {"metric": "fused adaLN chain (config 1) ms/step", "value": round(ms, 4), "unit": "ms/step",
                     "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
-                    "dtype": "bf16", "config": {"workload": "fused", "S": 32768, "D": 5120},
+                    "dtype": "bf16", "config": {"workload": "fused", "S": args.rows or 32768, "D": 5120},
                     "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
         else:
