@@ -274,15 +274,33 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
     return cfg, s_local, ms, clocks, spans, launches, e2e
 
 
-def gemm_roofline(spans, pk, src):
+def gemm_dram_traffic(shapes):
+    """DRAM bytes per GEMM launch: algorithmic bytes (A + B + bf16 out + scales + bias) of
+    the step's launches, scaled by the DRAM/algorithmic ratio of the ncu capture in
+    profiles/ncu_traffic.json (a smaller case of the same kernel; its traffic is
+    operand + output bytes, which grow in proportion)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            ratio = json.load(f)["gemm_i8_kernel"]["ratio"]
+    except (OSError, ValueError, KeyError):
+        return None, None
+    algo = [M * K + N * K + 2 * M * N + 4 * M + 6 * N for M, N, K in shapes]
+    return ratio * sum(algo) / len(algo), ratio
+
+
+def gemm_roofline(spans, pk, src, shapes=None):
     g = spans.get("gemm")
     if not g or g["ms"] <= 0:
         return None
     achieved = g["work"] / (g["ms"] * 1e-3) / 1e12  # TOPS
     peak = 2.0 * pk["bf16_tflops"]
+    traffic, ratio = gemm_dram_traffic(shapes) if shapes else (None, None)
     return {"kernel": "gemm_i8_kernel (tcgen05 kind::i8 + dequant epilogue)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
-            "frac": round(achieved / peak, 4), "traffic": None,
+            "frac": round(achieved / peak, 4), "traffic": None if traffic is None else int(traffic),
+            "traffic_note": None if ratio is None else
+            f"bytes per launch: algorithmic operand+output bytes x {ratio:.3f} (DRAM/algorithmic of the ncu "
+            "capture in profiles/gemm_i8_linear_m32768.md)",
             "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TFLOP/s burst; kind::i8 issues at "
                            "twice the kind::f16 rate on B200)",
             "work_per_step": g["work"], "launches_per_step": g["calls"], "ms_per_step": round(g["ms"], 3)}
@@ -497,14 +515,16 @@ def main():
                                "head_dim": cfg.head_dim, "ffn": cfg.ffn, "blocks": n_blocks, "text_len": text_len,
                                "parallelism": f"ulysses_sp{world}", "exchange": args.exchange if world > 1 else None,
                                "l2": "inputs larger than L2 (no flush)"},
-                    "roofline": gemm_roofline(spans, pk, pk_src), "clocks": clocks, "e2e": e2e,
+                    "roofline": gemm_roofline(spans, pk, pk_src, [(s_local, 3 * cfg.dim, cfg.dim), (s_local, cfg.dim, cfg.dim),
+                                                                  (s_local, cfg.ffn, cfg.dim), (s_local, cfg.dim, cfg.ffn)]),
+                    "clocks": clocks, "e2e": e2e,
                     "gpu_launches": int(round(launches * args.steps)), "breakdown": breakdown(spans, pk)}
             if rank == 0 and world == 1 and not args.no_cpu_baseline and not step_cfg:
                 line["cpu_baseline"] = cpu_baseline(cfg, seq)
         elif args.workload == "linear":
             ms, clocks, spans, launches = linear_workload(args, dev)
-            rl = gemm_roofline(spans, pk, pk_src)
             M = args.rows or 4096
+            rl = gemm_roofline(spans, pk, pk_src, [(M, 5120, 5120)])
             line = {"metric": "INT8 linear (config 0) TOPS", "value": round(2 * M * 5120 * 5120 / (ms * 1e-3) / 1e12, 1),
                     "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",

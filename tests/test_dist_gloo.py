@@ -1,0 +1,133 @@
+"""Multi-rank host logic on CPU: world_size 2 over gloo (no GPU).
+
+Covers the parts of the Ulysses path that are not kernels: SPContext's row
+splits, the exchange calls with their split sizes (h3b.sp._seq_gather /
+_seq_scatter, fed with oracle-packed buffers), the start-up known-answer probe,
+and failure detection -- a rank that never reaches the exchange makes the other
+rank's collective fail within the process-group timeout instead of hanging.
+"""
+import os
+import socket
+import sys
+import time
+import traceback
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _init(rank, world, port, timeout_s=60):
+    for p in (ROOT, os.path.join(ROOT, "minimax-h3-multi-dgx-spark_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=timeout_s))
+
+
+def _worker_exchange(rank, world, port, S, q):
+    try:
+        _init(rank, world, port)
+        from h3b import sp
+        from oracle import sp_layout
+        H, Dh = 8, 16
+        ctx = sp.SPContext(rank, world, dist.group.WORLD, S)
+        assert ctx.splits == sp_layout.splits(S, world)
+        assert ctx.start == sp_layout.starts(S, world)[rank]
+        # every rank draws all ranks' inputs from the same seeds -> local oracle
+        ts = [torch.randn(n, H, Dh, generator=torch.Generator().manual_seed(100 + r)).to(torch.bfloat16)
+              for r, n in enumerate(ctx.splits)]
+        bits = [t.view(torch.int16).numpy().view(np.uint16) for t in ts]
+        hp = H // world
+        # forward: pack (oracle) -> exchange (product host code) -> [S, hp, Dh]
+        # gloo has no 16-bit integer type: carry the bf16 bit patterns as float16
+        # (all_to_all copies bytes, the values are never interpreted)
+        send = torch.from_numpy(sp_layout.pack_fwd(bits[rank], world).view(np.float16)).reshape(-1)
+        out = torch.empty(S * hp * Dh, dtype=torch.float16)
+        sp._seq_gather(out, send, ctx, hp * Dh)
+        ref = sp_layout.a2a_fwd(bits, world)[rank]
+        np.testing.assert_array_equal(out.numpy().view(np.uint16).reshape(S, hp, Dh), ref)
+        # inverse: each rank's [S, hp*Dh] -> [s_local, H*Dh] after unpack (oracle)
+        outs = [torch.randn(S, hp * Dh, generator=torch.Generator().manual_seed(200 + r)).to(torch.bfloat16)
+                for r in range(world)]
+        obits = [o.view(torch.int16).numpy().view(np.uint16) for o in outs]
+        recv = torch.empty(world * ctx.local * hp * Dh, dtype=torch.float16)
+        sp._seq_scatter(recv, torch.from_numpy(obits[rank].view(np.float16)).reshape(-1), ctx, hp * Dh)
+        got = sp_layout.unpack_inv(recv.numpy().view(np.uint16).reshape(world, ctx.local, hp * Dh), world)
+        np.testing.assert_array_equal(got, sp_layout.a2a_inv(obits, world)[rank])
+        sp.startup_probe(rank, world, dist.group.WORLD, torch.device("cpu"))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+
+
+def _worker_dead_peer(rank, world, port, q):
+    try:
+        _init(rank, world, port, timeout_s=5)
+        from h3b import sp
+        ctx = sp.SPContext(rank, world, dist.group.WORLD, 100)
+        if rank == 1:
+            q.put((rank, "left"))  # leaves between steps, before the exchange, with nothing in flight
+            q.close()
+            q.join_thread()
+            os._exit(0)
+        send = torch.zeros(ctx.local * 4, dtype=torch.float32)
+        out = torch.empty(100 * 4, dtype=torch.float32)
+        t0 = time.time()
+        try:
+            sp._seq_gather(out, send, ctx, 4)
+            q.put((rank, "no error"))
+        except Exception as e:  # noqa: BLE001
+            q.put((rank, ("raised", time.time() - t0, type(e).__name__)))
+    except Exception:  # noqa: BLE001
+        q.put((rank, traceback.format_exc()))
+
+
+def _run(target, world, *args, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world, *args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    deadline = time.time() + timeout
+    while len(results) < world and time.time() < deadline:
+        try:
+            r, v = q.get(timeout=max(0.1, deadline - time.time()))
+            results[r] = v
+        except Exception:  # noqa: BLE001
+            break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+@pytest.mark.parametrize("S", [1001, 64])
+def test_exchange_world2_gloo(S):
+    res = _run(_worker_exchange, 2, _free_port(), S)
+    assert res == {0: "ok", 1: "ok"}, res
+
+
+def test_dead_peer_fails_within_timeout():
+    res = _run(_worker_dead_peer, 2, _free_port(), timeout=90)
+    assert res.get(1) == "left", res
+    r0 = res.get(0)
+    assert isinstance(r0, tuple) and r0[0] == "raised", res
+    assert r0[1] < 60, f"the surviving rank waited {r0[1]:.1f} s"
