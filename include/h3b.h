@@ -68,6 +68,14 @@ H3B_API int h3b_status_clear(void *stream);
  * the plain per-token absmax quantiser; the ConvRot rotation is not applied). */
 H3B_API int h3b_quant_rowwise(const void *x, int64_t ldx, int64_t M, int64_t K, int8_t *xq, float *xs, void *stream);
 
+/* GELU (tanh approximation, PyTorch's fp32 formula) fused into the quantiser:
+ * the codes / scales of bf16(gelu(u)) for u bf16 [M,K] (leading dimension ldu)
+ * -- the input of the FFN down projection -- without writing the activation.
+ * Equals h3b_quant_rowwise(F.gelu(u, approximate="tanh")) bit for bit.  The
+ * reference fuses its own activation (SwiGLU) into the quantiser the same way,
+ * h3_linear_fast_patch.py:3-5,93-95 (input_act). */
+H3B_API int h3b_gelu_quant(const void *u, int64_t ldu, int64_t M, int64_t K, int8_t *xq, float *xs, void *stream);
+
 /* INT8 GEMM with dequant epilogue on tcgen05 tensor cores:
  * acc[m,n] = sum_k xq[m,k] * w[n,k] (int32), out[m,n] =
  * bf16((float(acc) * xs[m]) * ws[n] [+ float(bias[n])]) with one rounding.
@@ -122,6 +130,22 @@ H3B_API int h3b_norm_mod(const void *x, const void *w, float eps, const int32_t 
  * Replaces gate_norm_mod_, h3_fuse_kernels.py:181-185 (kernel :117-155). */
 H3B_API int h3b_gate_norm_mod_(void *x, const void *o, const void *g, const void *w, float eps, const int32_t *ridx,
                        const void *s1, const void *sh, void *h, int64_t S, int64_t D, int64_t R, void *stream);
+
+/* norm_mod fused with the activation quantiser of the linear it feeds:
+ * instead of h, writes xq int8 [S,D] and xs fp32 [S] equal to
+ * h3b_quant_rowwise(h3b_norm_mod(...)) bit for bit (h never reaches HBM).
+ * D % 8 == 0, 16-byte aligned tensors.  Replaces the pair norm_mod
+ * (h3_fuse_kernels.py:174-178) -> quantiser call (h3_linear_fast_patch.py:89-95)
+ * at h3_fuse_patch.py:125 + sp_forward.py:280. */
+H3B_API int h3b_norm_mod_quant(const void *x, const void *w, float eps, const int32_t *ridx, const void *s1,
+                               const void *sh, int8_t *xq, float *xs, int64_t S, int64_t D, int64_t R, void *stream);
+
+/* gate_norm_mod_ fused with the quantiser: x <- bf16(x + o*g[r]) in place,
+ * then the int8 codes / scales of norm_mod(x) (h3_fuse_kernels.py:181-185 ->
+ * h3_linear_fast_patch.py:89-95, the MLP input at h3_fuse_patch.py:133-135). */
+H3B_API int h3b_gate_norm_mod_quant_(void *x, const void *o, const void *g, const void *w, float eps,
+                                     const int32_t *ridx, const void *s1, const void *sh, int8_t *xq, float *xs,
+                                     int64_t S, int64_t D, int64_t R, void *stream);
 
 /* x <- bf16(x + o * g[r]) in place.
  * Replaces gate_, h3_fuse_kernels.py:188-192 (kernel :158-167). */

@@ -59,8 +59,11 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ uint32_t f2bf_bits(float f) {
     return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
+// Two floats -> packed bf16x2 (lo in bits 0-15), round-to-nearest-even, one
+// paired conversion instead of two scalar ones.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    return f2bf_bits(lo) | (f2bf_bits(hi) << 16);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 // round to bf16 precision and return as float (the reference's _rbf16)
 __device__ __forceinline__ float rbf16(float f) { return __uint_as_float(f2bf_bits(f) << 16); }

@@ -13,7 +13,7 @@
 //   norm_mod       read x,   write h      4 B/element
 //   gate_norm_mod_ read x,o, write x,h    8 B/element
 //   gate_          read x,o, write x      6 B/element
-#include "common.cuh"
+#include "quant_common.cuh"
 
 namespace h3b {
 
@@ -156,6 +156,158 @@ __global__ void __launch_bounds__(128) gate_kernel(uint16_t* __restrict__ x, con
     }
 }
 
+// ---------------------------------------------------------------------------
+// 16-byte variant (D % 8 == 0): 64 threads per row.  Physical thread p holds the
+// two 4-element "virtual threads" 2p and 2p+1 of the 128-thread geometry above:
+// its 16-byte vector it*64 + p is exactly the 4-element vectors it*128 + 2p and
+// it*128 + 2p + 1.  Each virtual thread keeps its own accumulator (acc0 / acc1),
+// so the per-thread FMA order is unchanged; the virtual shuffle-down tree
+// 16, 8, 4, 2, 1 becomes physical shuffles 8, 4, 2, 1 inside 16-lane groups
+// followed by acc0 + acc1, and the four virtual warp sums sit at lanes 0 and 16
+// of the two physical warps.  Conversions to bf16 are paired
+// (cvt.rn.bf16x2.f32).  Q8 emits the row's int8 codes and fp32 scale instead of
+// h (the quantiser fused into its producer).
+constexpr int kNorm8Threads = 64;
+
+__device__ __forceinline__ uint32_t norm2(uint32_t xp, float rstd, uint32_t wp, uint32_t sp, uint32_t hp) {
+    const uint32_t y = pack_bf16x2(__fmul_rn(bf16_lo(wp), __fmul_rn(rstd, bf16_lo(xp))),
+                                   __fmul_rn(bf16_hi(wp), __fmul_rn(rstd, bf16_hi(xp))));
+    const uint32_t z = pack_bf16x2(__fmul_rn(bf16_lo(y), bf16_lo(sp)), __fmul_rn(bf16_hi(y), bf16_hi(sp)));
+    return pack_bf16x2(__fadd_rn(bf16_lo(z), bf16_lo(hp)), __fadd_rn(bf16_hi(z), bf16_hi(hp)));
+}
+
+__device__ __forceinline__ uint32_t gate2(uint32_t xp, uint32_t op, uint32_t gp) {
+    return pack_bf16x2(gate1(bf16_lo(xp), bf16_lo(op), bf16_lo(gp)), gate1(bf16_hi(xp), bf16_hi(op), bf16_hi(gp)));
+}
+
+__device__ __forceinline__ float sumsq2(uint32_t v, float acc) {
+    const float a = bf16_lo(v), b = bf16_hi(v);
+    acc = __fmaf_rn(a, a, acc);
+    return __fmaf_rn(b, b, acc);
+}
+
+template <int IT, bool GATE, bool Q8>
+__global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t* __restrict__ xq,
+                                                              float* __restrict__ xs) {
+    const int64_t row = blockIdx.x;
+    const int p = threadIdx.x, lane = p & 31, warp = p >> 5;
+    const int r = a.ridx[row];
+    if (r < 0 || r >= a.R) {
+        if (p == 0) report(a.status, H3B_STATUS_BAD_INDEX);
+        return;
+    }
+    const int nv = a.D >> 3;
+    uint4* xr = reinterpret_cast<uint4*>(a.x + row * (int64_t)a.D);
+    uint4 v[IT];
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+        const int j = it * kNorm8Threads + p;
+        if (j < nv) v[it] = xr[j];
+    }
+    if constexpr (GATE) {
+        const uint4* orow = reinterpret_cast<const uint4*>(a.o + row * (int64_t)a.D);
+        const uint4* grow = reinterpret_cast<const uint4*>(a.g + (int64_t)r * a.D);
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int j = it * kNorm8Threads + p;
+            if (j < nv) {
+                const uint4 o4 = orow[j], g4 = grow[j];
+                v[it] = make_uint4(gate2(v[it].x, o4.x, g4.x), gate2(v[it].y, o4.y, g4.y), gate2(v[it].z, o4.z, g4.z),
+                                   gate2(v[it].w, o4.w, g4.w));
+                xr[j] = v[it];
+            }
+        }
+    }
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+        const int j = it * kNorm8Threads + p;
+        if (j < nv) {
+            acc0 = sumsq2(v[it].y, sumsq2(v[it].x, acc0));
+            acc1 = sumsq2(v[it].w, sumsq2(v[it].z, acc1));
+        }
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        acc0 = __fadd_rn(acc0, __shfl_down_sync(0xffffffffu, acc0, off, 16));
+        acc1 = __fadd_rn(acc1, __shfl_down_sync(0xffffffffu, acc1, off, 16));
+    }
+    __shared__ float wsum[4];
+    __shared__ uint32_t wmax[2];
+    if ((lane & 15) == 0) wsum[warp * 2 + (lane >> 4)] = __fadd_rn(acc0, acc1);
+    __syncthreads();
+    const float tot = __fadd_rn(__fadd_rn(wsum[0], wsum[2]), __fadd_rn(wsum[1], wsum[3]));
+    const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.D), a.eps));
+
+    const uint4* wv = reinterpret_cast<const uint4*>(a.w);
+    const uint4* s1r = reinterpret_cast<const uint4*>(a.s1 + (int64_t)r * a.D);
+    const uint4* shr = reinterpret_cast<const uint4*>(a.sh + (int64_t)r * a.D);
+    uint4* hr = reinterpret_cast<uint4*>(a.h + row * (int64_t)a.D);
+    uint32_t m = 0;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+        const int j = it * kNorm8Threads + p;
+        if (j < nv) {
+            const uint4 w4 = wv[j], s4 = s1r[j], h4 = shr[j];
+            const uint4 y = make_uint4(norm2(v[it].x, rstd, w4.x, s4.x, h4.x), norm2(v[it].y, rstd, w4.y, s4.y, h4.y),
+                                       norm2(v[it].z, rstd, w4.z, s4.z, h4.z), norm2(v[it].w, rstd, w4.w, s4.w, h4.w));
+            if constexpr (Q8) {
+                v[it] = y;
+                m = absmax_bits8(y, m);
+            } else {
+                hr[j] = y;
+            }
+        }
+    }
+    if constexpr (Q8) {
+        uint32_t mb = __reduce_max_sync(0xffffffffu, max(m & 0xFFFFu, m >> 16));
+        if (lane == 0) wmax[warp] = mb;
+        __syncthreads();
+        mb = max(wmax[0], wmax[1]);
+        float sc, rc;
+        row_scale(__uint_as_float(mb << 16), sc, rc);
+        if (p == 0) xs[row] = sc;
+        uint2* qr = reinterpret_cast<uint2*>(xq + row * (int64_t)a.D);
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int j = it * kNorm8Threads + p;
+            if (j < nv) {
+                float f[8];
+                unpack8(v[it], f);
+                qr[j] = quant8(f, sc, rc);
+            }
+        }
+    }
+}
+
+template <bool GATE, bool Q8>
+static int launch_norm8(const NormArgs& a, int64_t S, int8_t* xq, float* xs, cudaStream_t s) {
+    const int need = (a.D / 8 + kNorm8Threads - 1) / kNorm8Threads;
+    static const int opts[] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 20, 24, 28, 32};
+    int it = -1;
+    for (int o : opts)
+        if (o >= need) {
+            it = o;
+            break;
+        }
+    dim3 grid((unsigned)S), block(kNorm8Threads);
+    switch (it) {
+#define H3B_N8(I) \
+    case I: norm8_kernel<I, GATE, Q8><<<grid, block, 0, s>>>(a, xq, xs); break;
+        H3B_N8(1) H3B_N8(2) H3B_N8(3) H3B_N8(4) H3B_N8(5) H3B_N8(6) H3B_N8(7) H3B_N8(8) H3B_N8(9) H3B_N8(10)
+        H3B_N8(11) H3B_N8(12) H3B_N8(13) H3B_N8(14) H3B_N8(15) H3B_N8(16) H3B_N8(20) H3B_N8(24) H3B_N8(28) H3B_N8(32)
+#undef H3B_N8
+        default: return set_error(H3B_ERR_UNSUPPORTED, "norm kernels: D=%d exceeds 16384", a.D);
+    }
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
+}
+
+static bool norm8_ok(const NormArgs& a) {
+    return a.D % 8 == 0 && aligned(a.x, 16) && aligned(a.w, 16) && aligned(a.s1, 16) && aligned(a.sh, 16) &&
+           (!a.h || aligned(a.h, 16)) && (!a.o || aligned(a.o, 16)) && (!a.g || aligned(a.g, 16));
+}
+
 template <bool GATE>
 static int launch_norm(const NormArgs& a, int64_t S, cudaStream_t s) {
     const int need = (a.D / 4 + kNormThreads - 1) / kNormThreads;
@@ -199,6 +351,7 @@ extern "C" int h3b_norm_mod(const void* x, const void* w, float eps, const int32
     NormArgs a{const_cast<uint16_t*>(static_cast<const uint16_t*>(x)), nullptr, nullptr,
                static_cast<const uint16_t*>(w), ridx, static_cast<const uint16_t*>(s1),
                static_cast<const uint16_t*>(sh), static_cast<uint16_t*>(h), eps, (int)D, (int)R, ds.word};
+    if (norm8_ok(a)) return launch_norm8<false, false>(a, S, nullptr, nullptr, static_cast<cudaStream_t>(stream));
     return launch_norm<false>(a, S, static_cast<cudaStream_t>(stream));
 }
 
@@ -213,6 +366,7 @@ extern "C" int h3b_gate_norm_mod_(void* x, const void* o, const void* g, const v
     NormArgs a{static_cast<uint16_t*>(x), static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(g),
                static_cast<const uint16_t*>(w), ridx, static_cast<const uint16_t*>(s1),
                static_cast<const uint16_t*>(sh), static_cast<uint16_t*>(h), eps, (int)D, (int)R, ds.word};
+    if (norm8_ok(a)) return launch_norm8<true, false>(a, S, nullptr, nullptr, static_cast<cudaStream_t>(stream));
     return launch_norm<true>(a, S, static_cast<cudaStream_t>(stream));
 }
 
@@ -235,4 +389,34 @@ extern "C" int h3b_gate_(void* x, const void* o, const void* g, const int32_t* r
                                                        static_cast<const uint16_t*>(g), ridx, (int)D, (int)R, ds.word);
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
+}
+
+extern "C" int h3b_norm_mod_quant(const void* x, const void* w, float eps, const int32_t* ridx, const void* s1,
+                                  const void* sh, int8_t* xq, float* xs, int64_t S, int64_t D, int64_t R,
+                                  void* stream) {
+    if (int rc = check_common(x, w, ridx, s1, sh, xq, S, D, R, "h3b_norm_mod_quant")) return rc;
+    H3B_REQUIRE(xs != nullptr, "h3b_norm_mod_quant: xs is NULL");
+    if (S == 0) return H3B_OK;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    NormArgs a{const_cast<uint16_t*>(static_cast<const uint16_t*>(x)), nullptr, nullptr,
+               static_cast<const uint16_t*>(w), ridx, static_cast<const uint16_t*>(s1),
+               static_cast<const uint16_t*>(sh), nullptr, eps, (int)D, (int)R, ds.word};
+    H3B_REQUIRE(norm8_ok(a), "h3b_norm_mod_quant: needs D %% 8 == 0 and 16-byte aligned tensors");
+    return launch_norm8<false, true>(a, S, xq, xs, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_gate_norm_mod_quant_(void* x, const void* o, const void* g, const void* w, float eps,
+                                        const int32_t* ridx, const void* s1, const void* sh, int8_t* xq, float* xs,
+                                        int64_t S, int64_t D, int64_t R, void* stream) {
+    if (int rc = check_common(x, w, ridx, s1, sh, xq, S, D, R, "h3b_gate_norm_mod_quant_")) return rc;
+    H3B_REQUIRE(o && g && xs, "h3b_gate_norm_mod_quant_: NULL pointer");
+    if (S == 0) return H3B_OK;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    NormArgs a{static_cast<uint16_t*>(x), static_cast<const uint16_t*>(o), static_cast<const uint16_t*>(g),
+               static_cast<const uint16_t*>(w), ridx, static_cast<const uint16_t*>(s1),
+               static_cast<const uint16_t*>(sh), nullptr, eps, (int)D, (int)R, ds.word};
+    H3B_REQUIRE(norm8_ok(a), "h3b_gate_norm_mod_quant_: needs D %% 8 == 0 and 16-byte aligned tensors");
+    return launch_norm8<true, true>(a, S, xq, xs, static_cast<cudaStream_t>(stream));
 }

@@ -1,72 +1,92 @@
-// a1: per-token absmax int8 quantisation of bf16 activations (HBM-bound).
+// a1: per-token absmax int8 quantisation of bf16 activations (HBM-bound),
+// optionally fused with the GELU(tanh) that feeds the FFN down projection.
 //
 // One CTA per row.  The row is read once with 16-byte vector loads and held in
-// registers (up to 16 vectors per thread); the absmax is reduced with warp
-// shuffles and a 4/8-entry shared-memory step (max is order-independent, so
-// the result is exact), then every element is divided by the fp32 scale with
-// IEEE division and rounded half-to-even.  Bytes per row: 2K read, K + 4 written.
-#include "common.cuh"
+// registers (up to 16 vectors per thread); the absmax is an unsigned max over
+// the bf16 bit patterns (warp redux + a shared-memory step, exact), then every
+// element is quantised with the reciprocal fast path of quant_common.cuh.
+// Bytes per row: 2K read, K + 4 written.
+//
+// GELU variant: each element first becomes bf16(gelu_tanh(x)) computed exactly
+// as PyTorch's GeluCUDAKernelImpl does in fp32 (x^3 as (x*x)*x, the inner
+// polynomial as one fused multiply-add, tanhf, 0.5*x*(1+t)), so the codes equal
+// quant(F.gelu(u, approximate="tanh")) bit for bit without the bf16 GELU output
+// ever reaching HBM.
+#include "quant_common.cuh"
 
 namespace h3b {
 
-template <int VPT, int NT>
+enum class Act { kNone = 0, kGeluTanh = 1 };
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    constexpr float kBeta = (float)(1.41421356237309504880 * 1.12837916709551257390 * 0.5);
+    constexpr float kKappa = (float)0.044715;
+    const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ uint32_t gelu2(uint32_t v) {
+    return pack_bf16x2(gelu_tanh(bf16_lo(v)), gelu_tanh(bf16_hi(v)));
+}
+
+template <int VPT, int NT, Act ACT>
 __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                                            int8_t* __restrict__ xq, float* __restrict__ xs) {
     const int64_t row = blockIdx.x;
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
     const int nvec = K >> 3;
     uint4 v[VPT];
-    float amax = 0.0f;
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int j = threadIdx.x + i * NT;
+        if (j < nvec) v[i] = xr[j];
+    }
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         const int j = threadIdx.x + i * NT;
         if (j < nvec) {
-            v[i] = xr[j];
-            const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                amax = fmaxf(amax, fmaxf(fabsf(bf16_lo(u[e])), fabsf(bf16_hi(u[e]))));
+            if constexpr (ACT == Act::kGeluTanh) {
+                v[i].x = gelu2(v[i].x);
+                v[i].y = gelu2(v[i].y);
+                v[i].z = gelu2(v[i].z);
+                v[i].w = gelu2(v[i].w);
+            }
+            m = absmax_bits8(v[i], m);
         }
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    __shared__ float wmax[NT / 32];
-    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+    uint32_t mb = max(m & 0xFFFFu, m >> 16);
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    __shared__ uint32_t wmax[NT / 32];
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mb;
     __syncthreads();
-    amax = wmax[0];
+    mb = wmax[0];
 #pragma unroll
-    for (int w = 1; w < NT / 32; ++w) amax = fmaxf(amax, wmax[w]);
+    for (int w = 1; w < NT / 32; ++w) mb = max(mb, wmax[w]);
 
-    const float sc = __fdiv_rn(amax, 127.0f);
-    if (threadIdx.x == 0) xs[row] = sc;
+    float s, r;
+    row_scale(__uint_as_float(mb << 16), s, r);
+    if (threadIdx.x == 0) xs[row] = s;
     uint2* qr = reinterpret_cast<uint2*>(xq + row * (int64_t)K);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         const int j = threadIdx.x + i * NT;
         if (j < nvec) {
-            const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
-            uint32_t packed[2] = {0u, 0u};
-            if (sc != 0.0f) {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float f = (e & 1) ? bf16_hi(u[e >> 1]) : bf16_lo(u[e >> 1]);
-                    int qv = __float2int_rn(__fdiv_rn(f, sc));
-                    qv = max(-127, min(127, qv));
-                    packed[e >> 2] |= (uint32_t)(qv & 0xFF) << (8 * (e & 3));
-                }
-            }
-            qr[j] = make_uint2(packed[0], packed[1]);
+            float f[8];
+            unpack8(v[i], f);
+            qr[j] = quant8(f, s, r);
         }
     }
 }
 
-template <int NT>
+template <int NT, Act ACT>
 static void launch_quant(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
                          cudaStream_t s) {
     dim3 grid((unsigned)M), block(NT);
     switch (vpt) {
 #define H3B_QCASE(V) \
-    case V: quant_rowwise_kernel<V, NT><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
+    case V: quant_rowwise_kernel<V, NT, ACT><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
         H3B_QCASE(1) H3B_QCASE(2) H3B_QCASE(3) H3B_QCASE(4) H3B_QCASE(5) H3B_QCASE(6) H3B_QCASE(7) H3B_QCASE(8)
         H3B_QCASE(10) H3B_QCASE(12) H3B_QCASE(14) H3B_QCASE(16)
 #undef H3B_QCASE
@@ -81,23 +101,31 @@ static int pick_vpt(int need) {
     return -1;
 }
 
-int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs, cudaStream_t s) {
-    H3B_REQUIRE(x && xq && xs, "h3b_quant_rowwise: NULL pointer");
-    H3B_REQUIRE(M >= 0 && K > 0 && K % 8 == 0 && K <= 32768, "h3b_quant_rowwise: K=%lld must be a positive multiple of 8 <= 32768", (long long)K);
-    H3B_REQUIRE(ldx >= K && ldx % 8 == 0 && aligned(x, 16), "h3b_quant_rowwise: x must be 16-byte aligned with ldx %% 8 == 0 (ldx=%lld)", (long long)ldx);
-    H3B_REQUIRE(aligned(xq, 8), "h3b_quant_rowwise: xq must be 8-byte aligned");
-    H3B_REQUIRE(M < (1ll << 31), "h3b_quant_rowwise: M too large");
+template <Act ACT>
+static int quant_impl(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs, cudaStream_t s,
+                      const char* who) {
+    H3B_REQUIRE(x && xq && xs, "%s: NULL pointer", who);
+    H3B_REQUIRE(M >= 0 && K > 0 && K % 8 == 0 && K <= 32768, "%s: K=%lld must be a positive multiple of 8 <= 32768", who,
+                (long long)K);
+    H3B_REQUIRE(ldx >= K && ldx % 8 == 0 && aligned(x, 16),
+                "%s: x must be 16-byte aligned with ldx %% 8 == 0 (ldx=%lld)", who, (long long)ldx);
+    H3B_REQUIRE(aligned(xq, 8), "%s: xq must be 8-byte aligned", who);
+    H3B_REQUIRE(M < (1ll << 31), "%s: M too large", who);
     if (M == 0) return H3B_OK;
     const int nvec = (int)(K / 8);
     int vpt = pick_vpt((nvec + 127) / 128);
     if (vpt > 0) {
-        launch_quant<128>(vpt, static_cast<const uint16_t*>(x), ldx, M, (int)K, xq, xs, s);
+        launch_quant<128, ACT>(vpt, static_cast<const uint16_t*>(x), ldx, M, (int)K, xq, xs, s);
     } else {
         vpt = pick_vpt((nvec + 255) / 256);
-        launch_quant<256>(vpt, static_cast<const uint16_t*>(x), ldx, M, (int)K, xq, xs, s);
+        launch_quant<256, ACT>(vpt, static_cast<const uint16_t*>(x), ldx, M, (int)K, xq, xs, s);
     }
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
+}
+
+int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs, cudaStream_t s) {
+    return quant_impl<Act::kNone>(x, ldx, M, K, xq, xs, s, "h3b_quant_rowwise");
 }
 
 }  // namespace h3b
@@ -105,4 +133,10 @@ int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, 
 extern "C" int h3b_quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs,
                                  void* stream) {
     return h3b::quant_rowwise(x, ldx, M, K, xq, xs, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_gelu_quant(const void* u, int64_t ldu, int64_t M, int64_t K, int8_t* xq, float* xs,
+                              void* stream) {
+    return h3b::quant_impl<h3b::Act::kGeluTanh>(u, ldu, M, K, xq, xs, static_cast<cudaStream_t>(stream),
+                                                "h3b_gelu_quant");
 }

@@ -1,0 +1,78 @@
+// Per-token int8 quantisation helpers shared by the quantiser and the fused
+// norm/GELU producers.
+//
+// q = clamp(rint_half_even(fl(x / s)), -127, 127), fl = IEEE fp32 division.
+// Fast path: t = fl(x * r) with r = fl(1 / s).  |t - x/s| <= |x/s| * 2^-22.9
+// and |fl(x/s) - x/s| <= 2^-18 for |x/s| <= 128, so |t - fl(x/s)| < 2^-15.
+// Whenever t is farther than 2^-14 from the half-integer between its two
+// neighbouring integers, rint(t) == rint(fl(x/s)); only inside that window
+// (about 1 element in 16k for smooth data) the exact division is done.
+// Everything per element runs on the FMA/ALU pipes (no conversion-unit op).
+#pragma once
+
+#include "common.cuh"
+
+namespace h3b {
+
+// Round-half-even of |t| < 2^22 on the FMA pipe: adding 1.5 * 2^23 leaves the
+// integer in the low mantissa bits (ties to even by the add's own rounding).
+// The low byte of the sum's bit pattern is the two's-complement low byte of
+// that integer, because 0x4B400000 has a zero low byte.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+// One element -> its int8 code in the low byte of the returned word.
+__device__ __forceinline__ uint32_t quant1(float x, float s, float r) {
+    const float t = __fmul_rn(x, r);
+    const float m = __fadd_rn(t, kRoundMagic);
+    const float n = __fsub_rn(m, kRoundMagic);
+    if (fabsf(__fsub_rn(t, n)) > 0.5f - 6.103515625e-05f /* 2^-14 */) {
+        // within reach of a half-integer: decide with the exact quotient
+        const float e = __fadd_rn(__fdiv_rn(x, s), kRoundMagic);
+        return __float_as_uint(e);
+    }
+    // |t| <= 127 by construction (|x| <= absmax), so the clamp to [-127, 127]
+    // of the reference formula never changes a code
+    return __float_as_uint(m);
+}
+
+// 8 values -> 8 int8 codes packed into two 32-bit words (s == 0 gives zeros)
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, float r) {
+    if (s == 0.0f) return make_uint2(0u, 0u);
+    uint32_t c[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) c[e] = quant1(v[e], s, r);
+    const uint32_t a = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+    const uint32_t b = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
+    return make_uint2(a, b);
+}
+
+// absmax of 8 bf16 values held as four bf16x2 words, as bf16 bits: for
+// non-negative finite bf16 the bit patterns order like the values, so the
+// max of |x| is an unsigned 16-bit max of (bits & 0x7FFF).
+__device__ __forceinline__ uint32_t absmax_bits8(uint4 v, uint32_t m) {
+    m = __vmaxu2(m, v.x & 0x7FFF7FFFu);
+    m = __vmaxu2(m, v.y & 0x7FFF7FFFu);
+    m = __vmaxu2(m, v.z & 0x7FFF7FFFu);
+    m = __vmaxu2(m, v.w & 0x7FFF7FFFu);
+    return m;
+}
+
+__device__ __forceinline__ float fold_absmax_bits(uint32_t m) {
+    const uint32_t b = max(m & 0xFFFFu, m >> 16);
+    return __uint_as_float(b << 16);
+}
+
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+    f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x);
+    f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+    f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z);
+    f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
+}
+
+// scale = absmax / 127 (IEEE) and its correctly rounded reciprocal
+__device__ __forceinline__ void row_scale(float amax, float& s, float& r) {
+    s = __fdiv_rn(amax, 127.0f);
+    r = s != 0.0f ? __frcp_rn(s) : 0.0f;
+}
+
+}  // namespace h3b

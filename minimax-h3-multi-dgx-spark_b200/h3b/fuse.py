@@ -58,6 +58,33 @@ def gate_norm_mod_(x, o, g, w, eps, ridx, s1, sh):
     return h
 
 
+def norm_mod_quant(x, w, eps, ridx, s1, sh):
+    """quant_rowwise(norm_mod(x, w, eps, ridx, s1, sh)) in one pass: (xq int8 [S,D], xs fp32 [S,1])."""
+    S, D, R = _check(x, w, ridx, s1, sh)
+    xq = torch.empty((S, D), dtype=torch.int8, device=x.device)
+    xs = torch.empty((S, 1), dtype=torch.float32, device=x.device)
+    with span("norm_mod_quant", 3 * S * D + 4 * S):
+        check(lib.h3b_norm_mod_quant(ptr(x), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh), ptr(xq), ptr(xs),
+                                     S, D, R, stream_of(x)), "h3b_norm_mod_quant")
+    return xq, xs
+
+
+def gate_norm_mod_quant_(x, o, g, w, eps, ridx, s1, sh):
+    """x <- bf16(x + o*g[r]) in place; returns quant_rowwise(norm_mod(x)) as (xq, xs)."""
+    S, D, R = _check(x, w, ridx, s1, sh)
+    require_cuda(o, g)
+    if o.shape != x.shape or o.dtype != BF16 or not o.is_contiguous():
+        raise ValueError("gate_norm_mod_quant_: o must match x")
+    if g.dtype != BF16 or tuple(g.shape) != (R, D) or not g.is_contiguous():
+        raise ValueError("gate_norm_mod_quant_: g must be a contiguous bf16 [R, D] table")
+    xq = torch.empty((S, D), dtype=torch.int8, device=x.device)
+    xs = torch.empty((S, 1), dtype=torch.float32, device=x.device)
+    with span("gate_norm_mod_quant_", 7 * S * D + 4 * S):
+        check(lib.h3b_gate_norm_mod_quant_(ptr(x), ptr(o), ptr(g), ptr(w), float(eps), ptr(ridx), ptr(s1), ptr(sh),
+                                           ptr(xq), ptr(xs), S, D, R, stream_of(x)), "h3b_gate_norm_mod_quant_")
+    return xq, xs
+
+
 def gate_(x, o, g, ridx):
     """x <- bf16(x + o * g[r]) in place; returns x."""
     require_cuda(x, o, g, ridx)

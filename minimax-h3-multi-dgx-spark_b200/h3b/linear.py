@@ -37,6 +37,21 @@ def quant_rowwise(x, xq=None, xs=None):
     return xq, xs
 
 
+def gelu_quant(u, xq=None, xs=None):
+    """quant_rowwise(F.gelu(u, approximate="tanh")) without materialising the GELU output."""
+    require_cuda(u)
+    if u.dtype != torch.bfloat16 or u.dim() != 2 or u.stride(1) != 1:
+        raise ValueError("gelu_quant: u must be a 2-D bf16 tensor with unit column stride")
+    M, K = u.shape
+    if xq is None:
+        xq = torch.empty((M, K), dtype=torch.int8, device=u.device)
+    if xs is None:
+        xs = torch.empty((M, 1), dtype=torch.float32, device=u.device)
+    with span("gelu_quant", 3 * M * K + 4 * M):
+        check(lib.h3b_gelu_quant(ptr(u), u.stride(0), M, K, ptr(xq), ptr(xs), stream_of(u)), "h3b_gelu_quant")
+    return xq, xs
+
+
 def _gemm_checks(xq, w):
     require_cuda(xq, w)
     if xq.dtype != torch.int8 or w.dtype != torch.int8 or xq.dim() != 2 or w.dim() != 2:

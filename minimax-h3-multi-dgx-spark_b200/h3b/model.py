@@ -9,6 +9,9 @@ configurations use a random-init stand-in with the same block structure:
       h = gate_norm_mod_(x, o, ga, w2, eps, ridx, s1m, shm)
       o = mlp(h)                            up INT8 linear -> GELU(tanh) -> down INT8 linear
       gate_(x, o, gm, ridx)
+  (with FUSED_PRODUCERS the norm kernels also quantise their output for the
+  INT8 linear they feed, and the GELU runs inside the down projection's
+  quantiser)
   sp_attention: qkv INT8 linear -> Ulysses forward all-to-all (q, k, v) ->
       SDPA over [1, H/P, S, Dh] -> inverse all-to-all -> out INT8 linear.
 
@@ -29,7 +32,10 @@ import torch
 import torch.nn.functional as F
 
 from . import fuse, sp
+from .linear import gelu_quant as _gelu_quant
+from .linear import int8_mm_scaled as _mm8
 from .linear import linear as _linear8
+from .linear import quant_rowwise as _quant
 
 BF16 = torch.bfloat16
 
@@ -100,6 +106,12 @@ def _lin(x, l):
     return _linear8(x, l.w, l.ws, l.b)
 
 
+def _lin_q(q, l):
+    """INT8 linear on already-quantised activations (codes, scales)."""
+    xq, xs = q
+    return _mm8(xq, l.w, xs, l.ws, bias=l.b)
+
+
 def sdpa_heads(q, k, v):
     """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h*Dh] via SDPA on [1, h, S, Dh] views."""
     o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
@@ -108,10 +120,11 @@ def sdpa_heads(q, k, v):
     return o.squeeze(0).transpose(0, 1).reshape(sq, h * dh)
 
 
-def self_attention(cfg, p, h, ctx):
-    s = h.shape[0]
+def self_attention(cfg, p, hq, ctx):
+    """hq: the quantised block input (codes, scales) of the modulated h."""
+    s = hq[0].shape[0]
     D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
-    qkv = _lin(h, p.qkv)  # [s, 3D]
+    qkv = _lin_q(hq, p.qkv)  # [s, 3D]
     q = qkv[:, :D].view(s, H, Dh)
     k = qkv[:, D:2 * D].view(s, H, Dh)
     v = qkv[:, 2 * D:].view(s, H, Dh)
@@ -123,10 +136,10 @@ def self_attention(cfg, p, h, ctx):
     return _lin(o, p.out)
 
 
-def cross_attention(cfg, p, h, text):
-    s = h.shape[0]
+def cross_attention(cfg, p, hq, text):
+    s = hq[0].shape[0]
     D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
-    q = _lin(h, p.cq).view(s, H, Dh)
+    q = _lin_q(hq, p.cq).view(s, H, Dh)
     kv = _lin(text, p.ckv)
     t = text.shape[0]
     k = kv[:, :D].view(t, H, Dh)
@@ -134,22 +147,37 @@ def cross_attention(cfg, p, h, text):
     return _lin(sdpa_heads(q, k, v), p.cout)
 
 
-def block_forward(cfg, p, x, ridx, ctx=None, text=None):
+# The modulated activations feed only INT8 linears, so the norm kernels can emit
+# their int8 codes and scales directly (norm_mod_quant / gate_norm_mod_quant_)
+# and the GELU can run inside the down projection's quantiser; results equal the
+# unfused sequence bit for bit.  The unfused kernels are faster today (the fused
+# ones are latency-bound at their register footprint), so they are the default.
+FUSED_PRODUCERS = False
+
+
+def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None):
     """One fused DiT block on the rank's rows x [s_local, D] (updated in place and returned)."""
+    fused = FUSED_PRODUCERS if fused_producers is None else fused_producers
     s1a, sha, ga, s1m, shm, gm = p.tables
-    h = fuse.norm_mod(x, p.n1w, cfg.eps, ridx, s1a, sha)
-    o = self_attention(cfg, p, h, ctx)
+    if fused:
+        hq = fuse.norm_mod_quant(x, p.n1w, cfg.eps, ridx, s1a, sha)
+    else:
+        hq = _quant(fuse.norm_mod(x, p.n1w, cfg.eps, ridx, s1a, sha))
+    o = self_attention(cfg, p, hq, ctx)
     if text is not None:
-        o = o + cross_attention(cfg, p, h, text)
-    del h
-    h = fuse.gate_norm_mod_(x, o, ga, p.n2w, cfg.eps, ridx, s1m, shm)
+        o = o + cross_attention(cfg, p, hq, text)
+    del hq
+    if fused:
+        hq = fuse.gate_norm_mod_quant_(x, o, ga, p.n2w, cfg.eps, ridx, s1m, shm)
+    else:
+        hq = _quant(fuse.gate_norm_mod_(x, o, ga, p.n2w, cfg.eps, ridx, s1m, shm))
     del o
-    u = _lin(h, p.up)
-    del h
-    a = F.gelu(u, approximate="tanh")
+    u = _lin_q(hq, p.up)
+    del hq
+    aq = _gelu_quant(u) if fused else _quant(F.gelu(u, approximate="tanh"))
     del u
-    m = _lin(a, p.down)
-    del a
+    m = _lin_q(aq, p.down)
+    del aq
     fuse.gate_(x, m, gm, ridx)
     return x
 

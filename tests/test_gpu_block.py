@@ -44,3 +44,18 @@ def test_block_full_width_one_frame():
 
 def test_block_with_text_cross_attention():
     _run(hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816, text_len=64), S=777, R=1, seed=5, text_len=64)
+
+
+def test_block_fused_producers_path():
+    """The block with the fused norm->quant and GELU->quant producers is bit-exact too."""
+    cfg = hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816)
+    p = hm.make_params(cfg, 0, 9, DEV, R=2)
+    x = randn_bf16((900, cfg.dim), 9).to(DEV)
+    ridx = torch.zeros(900, dtype=torch.int32, device=DEV)
+    ridx[450:] = 1
+    y = hm.block_forward(cfg, p, x.clone(), ridx, fused_producers=True)
+    y2 = hm.block_forward(cfg, p, x.clone(), ridx, fused_producers=False)
+    y_ref = tp.block_forward(cfg, p, x.clone(), ridx)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    assert torch.equal(y2.view(torch.int16), y_ref.view(torch.int16))

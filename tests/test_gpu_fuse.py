@@ -145,3 +145,34 @@ def test_bad_row_index_is_reported():
     assert h3b.status() == h3b._lib.STATUS_BAD_INDEX
     h3b.clear_status()
     assert h3b.status() == 0
+
+
+@pytest.mark.parametrize("S,D,R,adv", [(4096, 5120, 2, True), (257, 5376, 1, False), (64, 1000, 3, False)])
+def test_norm_mod_quant_equals_composition(S, D, R, adv):
+    """The fused producer's codes/scales equal quant_rowwise(norm_mod(x)) bit for bit."""
+    x, o, w, s1, sh, gt, ridx = _case(S, D, R, seed=7 * S + D, adversarial=adv)
+    xd, wd, s1d, shd, rd, od, gd = (t.to(DEV) for t in (x, w, s1, sh, ridx, o, gt))
+    q, s = h3b.norm_mod_quant(xd, wd, 1e-6, rd, s1d, shd)
+    q_ref, s_ref = h3b.quant_rowwise(h3b.norm_mod(xd, wd, 1e-6, rd, s1d, shd))
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+    x1, x2 = xd.clone(), xd.clone()
+    q, s = h3b.gate_norm_mod_quant_(x1, od, gd, wd, 1e-6, rd, s1d, shd)
+    q_ref, s_ref = h3b.quant_rowwise(h3b.gate_norm_mod_(x2, od, gd, wd, 1e-6, rd, s1d, shd))
+    torch.cuda.synchronize()
+    assert torch.equal(x1.view(torch.int16), x2.view(torch.int16))
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+
+
+@pytest.mark.parametrize("S,D", [(300, 1004), (64, 5124)])
+def test_norm_fallback_kernel_d_mod8_4(S, D):
+    """D % 8 == 4 takes the 8-byte-vector kernels; still bit-exact vs eager."""
+    x, o, w, s1, sh, gt, ridx = _case(S, D, 2, seed=S + 3 * D)
+    xd, od, wd, s1d, shd, gd, rd = (t.to(DEV) for t in (x, o, w, s1, sh, gt, ridx))
+    h = h3b.norm_mod(xd, wd, 1e-6, rd, s1d, shd)
+    assert torch.equal(h.view(torch.int16), _eager_norm_mod(xd, wd, 1e-6, rd, s1d, shd).view(torch.int16))
+    x_ref = xd.clone()
+    x_ref.addcmul_(od, gd[rd.long()])
+    h2 = h3b.gate_norm_mod_(xd, od, gd, wd, 1e-6, rd, s1d, shd)
+    assert torch.equal(xd.view(torch.int16), x_ref.view(torch.int16))
+    assert torch.equal(h2.view(torch.int16), _eager_norm_mod(x_ref, wd, 1e-6, rd, s1d, shd).view(torch.int16))

@@ -115,3 +115,34 @@ def test_rejects_bad_shapes():
         h3b.int8_mm_i32(xq, w)  # K % 128 != 0
     with pytest.raises(TypeError):
         h3b.quant_rowwise(torch.zeros(4, 16, dtype=torch.bfloat16))  # CPU tensor: no CPU path
+
+
+@pytest.mark.parametrize("M,K,scale", [(4096, 13824, 3.0), (513, 5120, 0.3), (64, 128, 20.0)])
+def test_gelu_quant_equals_torch_gelu_then_quant(M, K, scale):
+    """GELU(tanh) fused into the quantiser == quant_rowwise(F.gelu(u, "tanh")) with
+    PyTorch's own GELU on the GPU: any difference in the fp32 GELU arithmetic
+    would move codes across rounding boundaries somewhere in these rows."""
+    import torch.nn.functional as F
+    u = randn_bf16((M, K), seed=M + K, scale=scale).to(DEV)
+    q, s = h3b.gelu_quant(u)
+    q_ref, s_ref = h3b.quant_rowwise(F.gelu(u, approximate="tanh"))
+    torch.cuda.synchronize()
+    assert torch.equal(s, s_ref), "row scales differ (GELU maxima differ)"
+    assert torch.equal(q, q_ref), f"{(q != q_ref).sum().item()} codes differ"
+
+
+def test_quant_half_integer_ties():
+    """Rows whose quotients land exactly on (or next to) half-integers exercise the
+    exact-division fallback; codes must match the oracle (round half to even)."""
+    M, K = 64, 512
+    g = gen(99)
+    k = torch.randint(-126, 126, (M, K), generator=g).float()
+    x = (k + 0.5)
+    x[:, 0] = 127.0  # absmax 127 -> scale exactly 1, quotients exactly k + 0.5
+    x[32:, 0] = 126.0  # scale 126/127: quotients just off half-integers
+    x = x.to(torch.bfloat16)
+    q_ref, s_ref = oracle.quant_rowwise(bits(x))
+    xq, xs = h3b.quant_rowwise(x.to(DEV))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(xq.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(xs.cpu().numpy().reshape(-1), s_ref)
