@@ -24,6 +24,7 @@
 // H3B_STATUS_MBAR_TIMEOUT, stops issuing work, drains its own TMA loads and
 // MMAs (again bounded), frees TMEM and returns.
 #include <cuda.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -164,11 +165,59 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
     nb = r / gsize;
 }
 
+// Dequantise one 32-column chunk of one tile row (registers r) and store it:
+// out[row, col0 .. col0+31] = bf16((float(acc) * xs) * ws[n] [+ bias[n]]) with
+// separate IEEE products, or the raw int32 sums.  N % 8 == 0, so every 8-column
+// group is either fully inside or fully outside the matrix.
+template <bool OUT_I32>
+__device__ __forceinline__ void store_chunk(const Args& args, const uint32_t (&r)[32], int row, int col0, float xs) {
+    const int N = args.N;
+    if constexpr (OUT_I32) {
+        int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(args.out) + (int64_t)row * N + col0);
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+            if (col0 + 4 * g < N) dst[g] = make_int4((int)r[4 * g], (int)r[4 * g + 1], (int)r[4 * g + 2], (int)r[4 * g + 3]);
+    } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + (int64_t)row * N + col0);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const int cb = col0 + 8 * g;
+            if (cb >= N) break;
+            const float4 w0 = *reinterpret_cast<const float4*>(args.ws + cb);
+            const float4 w1 = *reinterpret_cast<const float4*>(args.ws + cb + 4);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            float bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (args.bias) {
+                const uint4 b = *reinterpret_cast<const uint4*>(args.bias + cb);
+                const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    bv[2 * e] = bf16_lo(bu[e]);
+                    bv[2 * e + 1] = bf16_hi(bu[e]);
+                }
+            }
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float v0 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e]), xs), wv[2 * e]);
+                float v1 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e + 1]), xs), wv[2 * e + 1]);
+                if (args.bias) {
+                    v0 = __fadd_rn(v0, bv[2 * e]);
+                    v1 = __fadd_rn(v1, bv[2 * e + 1]);
+                }
+                o[e] = pack_bf16x2(v0, v1);
+            }
+            dst[g] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 
 template <bool OUT_I32>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
+    gemm_i8_kernel(
+const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = base;
@@ -321,46 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col0 >= N) break;  // warp-uniform
                 uint32_t r[32];
                 tmem_ld32(t_row + (uint32_t)(c * 32), r);
-                if (!row_ok) continue;
-                if constexpr (OUT_I32) {
-                    int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(args.out) + (int64_t)row * N + col0);
-#pragma unroll
-                    for (int g = 0; g < 8; ++g)
-                        if (col0 + 4 * g < N)
-                            dst[g] = make_int4((int)r[4 * g], (int)r[4 * g + 1], (int)r[4 * g + 2], (int)r[4 * g + 3]);
-                } else {
-                    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(args.out) + (int64_t)row * N + col0);
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const int cb = col0 + 8 * g;
-                        if (cb >= N) break;
-                        const float4 w0 = *reinterpret_cast<const float4*>(args.ws + cb);
-                        const float4 w1 = *reinterpret_cast<const float4*>(args.ws + cb + 4);
-                        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                        float bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                        if (args.bias) {
-                            const uint4 b = *reinterpret_cast<const uint4*>(args.bias + cb);
-                            const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                bv[2 * e] = bf16_lo(bu[e]);
-                                bv[2 * e + 1] = bf16_hi(bu[e]);
-                            }
-                        }
-                        uint32_t o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            float v0 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e]), xs), wv[2 * e]);
-                            float v1 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e + 1]), xs), wv[2 * e + 1]);
-                            if (args.bias) {
-                                v0 = __fadd_rn(v0, bv[2 * e]);
-                                v1 = __fadd_rn(v1, bv[2 * e + 1]);
-                            }
-                            o[e] = pack_bf16x2(v0, v1);
-                        }
-                        dst[g] = make_uint4(o[0], o[1], o[2], o[3]);
-                    }
-                }
+                if (row_ok) store_chunk<OUT_I32>(args, r, row, col0, xs);
             }
             tc_fence_before();
             __syncwarp();
@@ -375,6 +385,254 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                      : "memory");
 }
+
+// ---------------------------------------------------------------------------
+// 2-CTA variant (cluster of 2, tcgen05 cta_group::2).  A pair of CTAs owns a
+// 256 x 256 output tile: CTA rank c loads rows [c*128, c*128+128) of the
+// tile's A rows AND rows [c*128, c*128+128) of its B rows (plain TMA into its
+// own shared memory; the .cta_group::2 load form lets both CTAs signal the
+// leader's stage barrier).  The leader (rank 0) issues
+// tcgen05.mma.cta_group::2 M=256 N=256 K=32, which reads A and B halves from
+// both CTAs and accumulates rows c*128.. into CTA c's TMEM.  Per SM this moves
+// 32 KiB per 128-byte k-block instead of 48 KiB, cutting L2->SM traffic by a
+// third.  Commits multicast to both CTAs' barriers; both CTAs' epilogue warps
+// release an accumulator on the leader's barrier.  No TMA multicast is used.
+namespace pair {
+
+constexpr int BM = 128;  // A rows per CTA; the pair tile has 256
+constexpr int TILE_M = 256;
+constexpr int TILE_N = 256;
+constexpr int B_ROWS = 128;  // B rows per CTA
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK;
+constexpr int B_BYTES = B_ROWS * BK;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_N >> 3) << 17) |
+                            ((uint32_t)(TILE_M >> 4) << 24);
+
+__device__ __forceinline__ uint32_t ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(mbar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+// arrive (when the MMAs issued so far complete) on `bar` in both CTAs of the pair
+__device__ __forceinline__ void umma_commit_both(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+template <bool OUT_I32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = base;
+    uint8_t* sB = base + STAGES * A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + NUM_ACC;
+    uint64_t* drain = tempty + NUM_ACC;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = ctarank();
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < NUM_ACC; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
+    }
+    if (warp == 1) {
+        // one warp with the same warp id in each CTA of the pair, same slot offset
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // barrier inits and the TMEM allocation are visible to both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int M = args.M, N = args.N, K = args.K;
+    const int m_tiles = (M + TILE_M - 1) / TILE_M, n_tiles = (N + TILE_N - 1) / TILE_N;
+    const int num_tiles = m_tiles * n_tiles;
+    const int kblocks = K / BK;
+    const int pair_id = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs; the leader also arms the stage barrier)
+            int stage = 0;
+            uint32_t phase = 0;
+            int armed = 0;
+            bool ok = true;
+            for (int tile = pair_id; ok && tile < num_tiles; tile += n_pairs) {
+                int mb, nb;
+                tile_coords(tile, m_tiles, n_tiles, mb, nb);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                    const uint32_t fb = mapa(smem_u32(&full[stage]), 0);
+                    tma_load_2d(sA + stage * A_BYTES, &tmA, fb, kb * BK, mb * TILE_M + (int)rank * BM);
+                    tma_load_2d(sB + stage * B_BYTES, &tmB, fb, kb * BK, nb * TILE_N + (int)rank * B_ROWS);
+                    ++armed;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                if (leader) {
+                    // the leader's stage barriers count both CTAs' bytes: wait (bounded)
+                    // until the armed stages have landed
+                    int s = stage;
+                    uint32_t p = phase;
+                    for (int i = 0; i < STAGES && i < armed; ++i) {
+                        if (--s < 0) {
+                            s = STAGES - 1;
+                            p ^= 1u;
+                        }
+                        volatile int no_abort = 0;
+                        mbar_wait(&full[s], p, &no_abort, nullptr, 100ull * 1000 * 1000);
+                    }
+                } else {
+                    const uint64_t t0 = globaltimer_ns();  // let this CTA's loads in flight land
+                    while (globaltimer_ns() - t0 < 2000000ull) __nanosleep(1000);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader CTA only)
+            int stage = 0;
+            uint32_t phase = 0;
+            int t = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int tile = pair_id; ok && tile < num_tiles; tile += n_pairs, ++t) {
+                const int acc = t & 1;
+                const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, args.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TILE_N);
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, args.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
+                        umma_i8(d_tmem, smem_desc(a0 + kk * UMMA_K), smem_desc(b0 + kk * UMMA_K), (kb | kk) != 0);
+                    issued = true;
+                    umma_commit_both(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (ok) umma_commit_both(&tfull[acc]);
+            }
+            if (!ok && issued) {
+                umma_commit_both(drain);
+                volatile int no_abort = 0;
+                mbar_wait(drain, 0, &no_abort, nullptr, 100ull * 1000 * 1000);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..5 (both CTAs: rows rank*128 .. of the pair tile)
+        const int q = warp & 3;
+        int t = 0;
+        for (int tile = pair_id; tile < num_tiles; tile += n_pairs, ++t) {
+            int mb, nb;
+            tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            const int acc = t & 1;
+            const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status)) break;
+            tc_fence_after();
+            const int row = mb * TILE_M + (int)rank * BM + q * 32 + lane;
+            const bool row_ok = row < M;
+            float xs = 0.0f;
+            if constexpr (!OUT_I32) xs = row_ok ? args.xs[row] : 0.0f;
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
+#pragma unroll 1
+            for (int c = 0; c < TILE_N / 32; ++c) {
+                const int col0 = nb * TILE_N + c * 32;
+                if (col0 >= N) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld32(t_row + (uint32_t)(c * 32), r);
+                if (row_ok) store_chunk<OUT_I32>(args, r, row, col0, xs);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(mapa(smem_u32(&tempty[acc]), 0));
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // both CTAs are done with TMEM (every MMA was consumed by an epilogue)
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+}
+
+}  // namespace pair
 
 // ---------------------------------------------------------------------------
 // Host side
@@ -417,6 +675,39 @@ static int num_sms() {
     return sms;
 }
 
+// H3B_GEMM_SINGLE_CTA=1 selects the 1-CTA kernel for every shape (the 2-CTA
+// kernel is the default when M > 128).
+static bool force_single_cta() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("H3B_GEMM_SINGLE_CTA");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
+// How many CTA pairs can be resident at once (a GPC may not pair every SM);
+// queried once per device and kernel variant, SM count / 2 if the query fails.
+template <bool OUT_I32>
+static int max_pairs() {
+    constexpr int kMaxDevices = 64;
+    static int cache[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return num_sms() / 2;
+    if (cache[dev] > 0) return cache[dev];
+    int n = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = pair::kSmemBytes;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)pair::gemm_i8_pair_kernel<OUT_I32>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = num_sms() / 2;
+    }
+    cache[dev] = n;
+    return n;
+}
+
 static int check_device() {
     int dev = 0, major = 0;
     H3B_CUDA_TRY(cudaGetDevice(&dev));
@@ -444,10 +735,21 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
     DeviceStatus ds;
     if (int rc = device_status(&ds)) return rc;
     a.status = ds.word;
-    H3B_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-    const int64_t tiles = (int64_t)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
-    const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
-    gemm_i8_kernel<OUT_I32><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, a);
+    if (a.M > BM && !force_single_cta()) {
+        // 2-CTA pairs: B is tiled 128 rows per CTA
+        if (int rc = make_map(&tmB, w, a.N, a.K, pair::B_ROWS)) return rc;
+        H3B_CUDA_TRY(cudaFuncSetAttribute(pair::gemm_i8_pair_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          pair::kSmemBytes));
+        const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + pair::TILE_N - 1) / pair::TILE_N);
+        const int64_t pairs_max = max_pairs<OUT_I32>();
+        const int pairs = (int)(tiles < pairs_max ? tiles : pairs_max);
+        pair::gemm_i8_pair_kernel<OUT_I32><<<2 * pairs, kThreads, pair::kSmemBytes, s>>>(tmA, tmB, a);
+    } else {
+        H3B_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        const int64_t tiles = (int64_t)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
+        const int grid = (int)(tiles < num_sms() ? tiles : num_sms());
+        gemm_i8_kernel<OUT_I32><<<grid, kThreads, kSmemBytes, s>>>(tmA, tmB, a);
+    }
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
 }

@@ -39,7 +39,8 @@ def test_quant_bit_exact(M, K):
     np.testing.assert_array_equal(xs.cpu().numpy().reshape(-1), s_ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (129, 264, 384), (300, 8, 128), (40, 48, 256), (256, 512, 1024)])
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (129, 264, 384), (300, 8, 128), (40, 48, 256), (256, 512, 1024),
+                                   (257, 520, 256), (128, 264, 384), (513, 776, 640)])
 def test_gemm_small_vs_oracle(M, N, K):
     g = gen(M + N + K)
     xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
@@ -77,7 +78,8 @@ def test_gemm_golden_inputs(golden_dir, name):
     np.testing.assert_array_equal(bits(y), oracle.int8_mm_scaled(d["xq"], d["w"], d["xs"], d["ws"]))
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 5120, 5120), (1000, 15360, 5120), (777, 5120, 13824), (16000, 5120, 5120)])
+@pytest.mark.parametrize("M,N,K", [(4096, 5120, 5120), (1000, 15360, 5120), (777, 5120, 13824), (16000, 5120, 5120),
+                                   (128, 5120, 5120), (100, 15360, 5120), (32768, 5120, 5120)])
 def test_gemm_large_vs_cublas(M, N, K):
     g = gen(M ^ N ^ K)
     xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(DEV)
