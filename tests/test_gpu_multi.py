@@ -1,6 +1,7 @@
-"""Ulysses exchange and the SP block on 2 GPUs (one spawned process per GPU, NCCL).
+"""Ulysses exchange and the SP block on 2, 4 and 8 GPUs (one spawned process per GPU, NCCL).
 
-Skipped on hosts with fewer than 2 GPUs.  Each rank draws every rank's inputs
+Each world size runs when the host has that many GPUs (skipped otherwise).
+Each rank draws every rank's inputs
 from the same seeds, so it can check its own result against the numpy
 restatement locally.  Checked bit-exactly:
   * the start-up known-answer probe (sp_group.py:107-128);
@@ -8,7 +9,7 @@ restatement locally.  Checked bit-exactly:
     all_to_all_single, unpack kernel) and peer-memory back end (fused p2p
     kernels + flag barriers), with an uneven row split;
   * the same exchanges done the reference's way (reshape + all_to_all_single);
-  * one full DiT block at world 2 (p2p exchange) against the eager PyTorch
+  * one full DiT block (p2p exchange) against the eager PyTorch
     block using all_to_all_single.
 """
 import os
@@ -57,7 +58,7 @@ def _worker(rank, world, port, q):
         g = dist.group.WORLD
         h3b.startup_probe(rank, world, g, dev)
         H, Dh = 40, 128
-        for S in (1001, 8192):
+        for S in (1001 + world, 8192):
             splits = sp_layout.splits(S, world)
             hp = H // world
             ins = [[torch.randn(splits[r], H, Dh, generator=torch.Generator().manual_seed(10 * i + r)).to(torch.bfloat16)
@@ -84,7 +85,7 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize(dev)
             dist.barrier(device_ids=[rank])
             peer.close()
-        # one full block at world 2 against the eager block
+        # one full block at this world size against the eager block
         cfg = hm.DiTConfig()
         S = 4128
         p = hm.make_params(cfg, 0, 7, dev, R=2)
@@ -108,9 +109,11 @@ def _worker(rank, world, port, q):
         q.put((rank, traceback.format_exc()))
 
 
-def test_exchange_and_block_world2():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_exchange_and_block(world):
     import torch.multiprocessing as mp
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -129,4 +132,4 @@ def test_exchange_and_block_world2():
         p.join(timeout=60)
         if p.is_alive():
             p.kill()
-    assert res == {0: "ok", 1: "ok"}, res
+    assert res == {r: "ok" for r in range(world)}, res
