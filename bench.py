@@ -295,12 +295,12 @@ def gemm_roofline(spans, pk, src, shapes=None):
     achieved = g["work"] / (g["ms"] * 1e-3) / 1e12  # TOPS
     peak = 2.0 * pk["bf16_tflops"]
     traffic, ratio = gemm_dram_traffic(shapes) if shapes else (None, None)
-    return {"kernel": "gemm_i8_kernel (tcgen05 kind::i8 + dequant epilogue)", "bound": "tensor",
+    return {"kernel": "gemm_i8_pair_kernel (tcgen05 cta_group::2 kind::i8 + dequant epilogue)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
             "frac": round(achieved / peak, 4), "traffic": None if traffic is None else int(traffic),
             "traffic_note": None if ratio is None else
             f"bytes per launch: algorithmic operand+output bytes x {ratio:.3f} (DRAM/algorithmic of the ncu "
-            "capture in profiles/gemm_i8_linear_m32768.md)",
+            "capture in profiles/gemm_i8_pair_linear_m32768.md)",
             "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TFLOP/s burst; kind::i8 issues at "
                            "twice the kind::f16 rate on B200)",
             "work_per_step": g["work"], "launches_per_step": g["calls"], "ms_per_step": round(g["ms"], 3)}

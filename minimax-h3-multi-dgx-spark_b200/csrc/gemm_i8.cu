@@ -59,6 +59,7 @@ struct Args {
     void* out;
     int M, N, K;
     int* status;
+    int tile_n;  // 2-CTA kernel: output tile width (multiple of 32, <= 256)
 };
 
 // ---------------------------------------------------------------------------
@@ -388,11 +389,12 @@ const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB
 
 // ---------------------------------------------------------------------------
 // 2-CTA variant (cluster of 2, tcgen05 cta_group::2).  A pair of CTAs owns a
-// 256 x 256 output tile: CTA rank c loads rows [c*128, c*128+128) of the
-// tile's A rows AND rows [c*128, c*128+128) of its B rows (plain TMA into its
+// 256 x tile_n output tile (tile_n = 32..256, chosen per launch): CTA rank c
+// loads rows [c*128, c*128+128) of the tile's A rows AND rows
+// [c*tile_n/2, (c+1)*tile_n/2) of its B rows (plain TMA into its
 // own shared memory; the .cta_group::2 load form lets both CTAs signal the
 // leader's stage barrier).  The leader (rank 0) issues
-// tcgen05.mma.cta_group::2 M=256 N=256 K=32, which reads A and B halves from
+// tcgen05.mma.cta_group::2 M=256 N=tile_n K=32, which reads A and B halves from
 // both CTAs and accumulates rows c*128.. into CTA c's TMEM.  Per SM this moves
 // 32 KiB per 128-byte k-block instead of 48 KiB, cutting L2->SM traffic by a
 // third.  Commits multicast to both CTAs' barriers; both CTAs' epilogue warps
@@ -401,15 +403,15 @@ namespace pair {
 
 constexpr int BM = 128;  // A rows per CTA; the pair tile has 256
 constexpr int TILE_M = 256;
-constexpr int TILE_N = 256;
-constexpr int B_ROWS = 128;  // B rows per CTA
+constexpr int MAX_TILE_N = 256;  // tile width is a launch parameter: 32..256, multiple of 32
+constexpr int B_ROWS = 128;      // B rows per CTA at the widest tile
 constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = B_ROWS * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_N >> 3) << 17) |
-                            ((uint32_t)(TILE_M >> 4) << 24);
+// instruction descriptor without its N field (bits 17-22 = N >> 3, set per launch)
+constexpr uint32_t kIdescBase = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_M >> 4) << 24);
 
 __device__ __forceinline__ uint32_t ctarank() {
     uint32_t r;
@@ -432,12 +434,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         "l"(map), "r"(mbar_cluster), "r"(c0), "r"(c1)
         : "memory");
 }
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 // arrive (when the MMAs issued so far complete) on `bar` in both CTAs of the pair
@@ -500,6 +503,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int M = args.M, N = args.N, K = args.K;
+    const int TILE_N = args.tile_n;
+    const int b_rows = TILE_N / 2;  // B rows this CTA loads
+    const uint32_t idesc = kIdescBase | ((uint32_t)(TILE_N >> 3) << 17);
+    const uint32_t stage_tx = 2u * (uint32_t)(A_BYTES + b_rows * BK);
     const int m_tiles = (M + TILE_M - 1) / TILE_M, n_tiles = (N + TILE_N - 1) / TILE_N;
     const int num_tiles = m_tiles * n_tiles;
     const int kblocks = K / BK;
@@ -520,10 +527,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                    if (leader) mbar_expect_tx(&full[stage], stage_tx);
                     const uint32_t fb = mapa(smem_u32(&full[stage]), 0);
                     tma_load_2d(sA + stage * A_BYTES, &tmA, fb, kb * BK, mb * TILE_M + (int)rank * BM);
-                    tma_load_2d(sB + stage * B_BYTES, &tmB, fb, kb * BK, nb * TILE_N + (int)rank * B_ROWS);
+                    tma_load_2d(sB + stage * B_BYTES, &tmB, fb, kb * BK, nb * TILE_N + (int)rank * b_rows);
                     ++armed;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -567,7 +574,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TILE_N);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MAX_TILE_N);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, args.status)) {
                         ok = false;
@@ -578,7 +585,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; ++kk)
-                        umma_i8(d_tmem, smem_desc(a0 + kk * UMMA_K), smem_desc(b0 + kk * UMMA_K), (kb | kk) != 0);
+                        umma_i8(d_tmem, smem_desc(a0 + kk * UMMA_K), smem_desc(b0 + kk * UMMA_K), idesc,
+                                (kb | kk) != 0);
                     issued = true;
                     umma_commit_both(&empty[stage]);
                     if (++stage == STAGES) {
@@ -609,7 +617,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool row_ok = row < M;
             float xs = 0.0f;
             if constexpr (!OUT_I32) xs = row_ok ? args.xs[row] : 0.0f;
-            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TILE_N);
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * MAX_TILE_N);
 #pragma unroll 1
             for (int c = 0; c < TILE_N / 32; ++c) {
                 const int col0 = nb * TILE_N + c * 32;
@@ -675,6 +683,38 @@ static int num_sms() {
     return sms;
 }
 
+// Output tile width of the 2-CTA kernel.  The kernel is bound by the L2->SM
+// feed (measured: throughput at width t scales as 1 / (8192/t + 32) bytes per
+// clock per SM), so a tile's run time is proportional to the operand rows it
+// streams per k-block, 256 (A) + t (B).  The chosen width minimises
+// (rounds of pair tiles over the resident pairs) x (256 + t); ties go to the
+// wider tile.  Wave quantisation picks 224 for config 0's 4096 x 5120; large M
+// keeps 256.
+static int pick_tile_n(int M, int N, int64_t pairs) {
+    // H3B_GEMM_TILE_N (a multiple of 32 in 32..256) pins the width, for tuning sweeps
+    static int forced = -1;
+    if (forced < 0) {
+        const char* e = getenv("H3B_GEMM_TILE_N");
+        const int v = e ? atoi(e) : 0;
+        forced = (v >= 32 && v <= 256 && v % 32 == 0) ? v : 0;
+    }
+    if (forced) return forced;
+    static const int cands[] = {256, 224, 192, 160, 128};
+    const int64_t m_tiles = (M + pair::TILE_M - 1) / pair::TILE_M;
+    int best = 256;
+    int64_t best_cost = -1;
+    for (int t : cands) {
+        const int64_t tiles = m_tiles * ((N + t - 1) / t);
+        const int64_t rounds = (tiles + pairs - 1) / pairs;
+        const int64_t cost = rounds * (256 + t);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = t;
+        }
+    }
+    return best;
+}
+
 // H3B_GEMM_SINGLE_CTA=1 selects the 1-CTA kernel for every shape (the 2-CTA
 // kernel is the default when M > 128).
 static bool force_single_cta() {
@@ -736,12 +776,13 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
     if (int rc = device_status(&ds)) return rc;
     a.status = ds.word;
     if (a.M > BM && !force_single_cta()) {
-        // 2-CTA pairs: B is tiled 128 rows per CTA
-        if (int rc = make_map(&tmB, w, a.N, a.K, pair::B_ROWS)) return rc;
+        // 2-CTA pairs: each CTA loads tile_n / 2 rows of B
         H3B_CUDA_TRY(cudaFuncSetAttribute(pair::gemm_i8_pair_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           pair::kSmemBytes));
-        const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + pair::TILE_N - 1) / pair::TILE_N);
         const int64_t pairs_max = max_pairs<OUT_I32>();
+        a.tile_n = pick_tile_n(a.M, a.N, pairs_max);
+        if (int rc = make_map(&tmB, w, a.N, a.K, (uint32_t)(a.tile_n / 2))) return rc;
+        const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + a.tile_n - 1) / a.tile_n);
         const int pairs = (int)(tiles < pairs_max ? tiles : pairs_max);
         pair::gemm_i8_pair_kernel<OUT_I32><<<2 * pairs, kThreads, pair::kSmemBytes, s>>>(tmA, tmB, a);
     } else {
