@@ -61,6 +61,9 @@ def parse_args():
     ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
     ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / S of the fused workload")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default=os.environ.get("H3B_EXCHANGE", "p2p"))
+    ap.add_argument("--overlap", type=int, default=None,
+                    help="head groups of the exchange/attention overlap (default: H3B_SP_OVERLAP_GROUPS or the "
+                         "reference's MINIMAX_SP_OVERLAP_CHUNKS; 0 = off)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -211,11 +214,23 @@ def seeded_rows(start, stop, dim, seed, dtype=torch.bfloat16):
 # ---------------------------------------------------------------------------
 # DiT block / step workload
 
+def overlap_groups(cfg, world):
+    """Head groups the block's attention uses (0: exchange and attention in sequence)."""
+    if world == 1:
+        return 0
+    from h3b import sp
+    hp = cfg.heads // world
+    n = sp.overlap_groups(hp, world)
+    return n if n > 1 and hp % n == 0 else 0
+
+
 def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
     import h3b
     from h3b import model as hm
     from h3b.trace import Trace
 
+    if args.overlap is not None:
+        os.environ["H3B_SP_OVERLAP_GROUPS"] = str(args.overlap)
     cfg = hm.DiTConfig(n_blocks=n_blocks, text_len=text_len)
     dit = hm.SynthDiT(cfg, dev, seed=1)
     peer = None
@@ -514,6 +529,7 @@ def main():
                                "local_rows": s_local, "dim": cfg.dim, "heads": cfg.heads,
                                "head_dim": cfg.head_dim, "ffn": cfg.ffn, "blocks": n_blocks, "text_len": text_len,
                                "parallelism": f"ulysses_sp{world}", "exchange": args.exchange if world > 1 else None,
+                               "overlap_groups": overlap_groups(cfg, world),
                                "l2": "inputs larger than L2 (no flush)"},
                     "roofline": gemm_roofline(spans, pk, pk_src, [(s_local, 3 * cfg.dim, cfg.dim), (s_local, cfg.dim, cfg.dim),
                                                                   (s_local, cfg.ffn, cfg.dim), (s_local, cfg.dim, cfg.ffn)]),

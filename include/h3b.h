@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define H3B_ABI_VERSION 1
+#define H3B_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define H3B_API __attribute__((visibility("default")))
@@ -154,18 +154,27 @@ H3B_API int h3b_gate_(void *x, const void *o, const void *g, const int32_t *ridx
 
 /* ---- Ulysses all-to-all -------------------------------------------------- */
 
-/* Forward pack: t [s_local, P * chunk] (row stride t_ld bytes) -> send
- * [P, s_local, chunk] (chunk = (H/P)*Dh elements, given in bytes).  The NCCL
- * exchange that follows receives [S, chunk] already in sequence order.
+/* Forward pack: rows of t (row stride t_ld bytes) hold one block of
+ * block_bytes per destination rank; the first chunk_bytes of block j of row s
+ * go to send[j, s, :] (send is [P, s_local, chunk]).  block = chunk is the
+ * whole exchange (t [s_local, P * chunk], chunk = (H/P)*Dh elements); a head
+ * group of each rank's heads is a narrower chunk with t offset to the group's
+ * first column.  The NCCL exchange that follows receives [S, chunk] already in
+ * sequence order.
  * Replaces t.reshape(s_local, p, chunk).transpose(0, 1).contiguous() of
- * comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:185. */
-H3B_API int h3b_a2a_pack(const void *t, int64_t t_ld, void *send, int64_t s_local, int64_t chunk_bytes, int world,
-                         void *stream);
+ * comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:185 and the per-group
+ * prep() of sp_attention_overlap, sp_forward.py:222-224. */
+H3B_API int h3b_a2a_pack(const void *t, int64_t t_ld, void *send, int64_t s_local, int64_t chunk_bytes,
+                         int64_t block_bytes, int world, void *stream);
 
-/* Inverse unpack: recv [P, s_local, chunk] -> out [s_local, P * chunk].
+/* Inverse unpack: recv [P, s_local, chunk] -> row s of out (row stride out_ld
+ * bytes), bytes [j*block, j*block + chunk) <- recv[j, s, :].  block = chunk,
+ * out_ld = P*chunk is out [s_local, P * chunk]; a head group writes a narrower
+ * chunk at its column offset (out offset by the caller).
  * Replaces out.view(p, s_local, chunk).transpose(0, 1).reshape(...) of
- * sp_forward.py:198. */
-H3B_API int h3b_a2a_unpack(const void *recv, void *out, int64_t s_local, int64_t chunk_bytes, int world, void *stream);
+ * sp_forward.py:198 and final[:, :, i] = ... of sp_forward.py:257-258. */
+H3B_API int h3b_a2a_unpack(const void *recv, void *out, int64_t out_ld, int64_t s_local, int64_t chunk_bytes,
+                           int64_t block_bytes, int world, void *stream);
 
 /* CUDA IPC plumbing for the peer-memory all-to-all.  h3b_ipc_handle returns
  * the 64-byte cudaIpcMemHandle of the allocation holding dev_ptr and
@@ -187,20 +196,26 @@ H3B_API int h3b_peer_barrier(uint32_t *const *peer_flags, int world, int rank, u
                      void *stream);
 
 /* Forward exchange fused with the pack, over peer memory: for each of n
- * tensors src[i] [s_local, P * chunk] (row stride src_ld bytes, shared by all
- * n) and each rank j, rows go straight into rank j's receive buffer
- * dst[i * P + j] ([S, chunk]) at rows row_start .. row_start + s_local.
- * Bracket with h3b_peer_barrier.
- * Replaces a2a_gather_seq_scatter_heads / _seq_gather, sp_forward.py:158-166,179-188. */
+ * tensors src[i] (rows of s_local, row stride src_ld bytes shared by all n)
+ * holding one block of block_bytes per destination rank j, the width_bytes at
+ * offset_bytes inside block j go straight into rank j's receive buffer
+ * dst[i * P + j] (rows of width_bytes) at rows row_start .. row_start + s_local.
+ * block = width, offset = 0 is the whole exchange; a head group of the heads
+ * rank j owns is a narrower width at an offset.  Bracket with h3b_peer_barrier.
+ * Replaces a2a_gather_seq_scatter_heads / _seq_gather, sp_forward.py:158-166,179-188,
+ * and the per-group exchanges of sp_attention_overlap, sp_forward.py:211-261. */
 H3B_API int h3b_a2a_fwd_p2p(int n, const void *const *src, int64_t src_ld, void *const *dst, int64_t s_local,
-                            int64_t row_start, int64_t chunk_bytes, int world, void *stream);
+                            int64_t row_start, int64_t width_bytes, int64_t block_bytes, int64_t offset_bytes,
+                            int world, void *stream);
 
-/* Inverse exchange fused with the unpack: src [S, chunk] rows (leading
- * dimension src_ld bytes) split by `splits` (P entries) go to rank j's
- * output dst[j] ([splits[j], P * chunk]) at column block `rank`.
+/* Inverse exchange fused with the unpack: src rows of width_bytes (leading
+ * dimension src_ld bytes, S = sum(splits) rows) split by `splits` (P entries)
+ * go to rank j's output dst[j] (rows dst_ld bytes apart) at byte column
+ * offset_bytes.  For the whole exchange: width = (H/P)*Dh*elt, dst_ld = P*width,
+ * offset = rank*width; a head group shifts the offset inside rank's block.
  * Replaces a2a_scatter_seq_gather_heads / _seq_scatter, sp_forward.py:169-176,191-198. */
-H3B_API int h3b_a2a_inv_p2p(const void *src, int64_t src_ld, void *const *dst, const int64_t *splits, int64_t chunk_bytes,
-                    int world, int rank, void *stream);
+H3B_API int h3b_a2a_inv_p2p(const void *src, int64_t src_ld, void *const *dst, const int64_t *splits,
+                            int64_t width_bytes, int64_t dst_ld, int64_t offset_bytes, int world, void *stream);
 
 #ifdef __cplusplus
 }

@@ -35,14 +35,14 @@ SIGNATURES = [
     ("h3b_norm_mod_quant", _I32, [_P, _P, _F32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_gate_norm_mod_quant_", _I32, [_P, _P, _P, _P, _F32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_gelu_quant", _I32, [_P, _I64, _I64, _I64, _P, _P, _P]),
-    ("h3b_a2a_pack", _I32, [_P, _I64, _P, _I64, _I64, _I32, _P]),
-    ("h3b_a2a_unpack", _I32, [_P, _P, _I64, _I64, _I32, _P]),
+    ("h3b_a2a_pack", _I32, [_P, _I64, _P, _I64, _I64, _I64, _I32, _P]),
+    ("h3b_a2a_unpack", _I32, [_P, _P, _I64, _I64, _I64, _I64, _I32, _P]),
     ("h3b_ipc_handle", _I32, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     ("h3b_ipc_open", _I32, [_P, _I64, _PP, _PP]),
     ("h3b_ipc_close", _I32, [_P]),
     ("h3b_peer_barrier", _I32, [_PP, _I32, _I32, _U32, _I64, _P]),
-    ("h3b_a2a_fwd_p2p", _I32, [_I32, _PP, _I64, _PP, _I64, _I64, _I64, _I32, _P]),
-    ("h3b_a2a_inv_p2p", _I32, [_P, _I64, _PP, ctypes.POINTER(ctypes.c_int64), _I64, _I32, _I32, _P]),
+    ("h3b_a2a_fwd_p2p", _I32, [_I32, _PP, _I64, _PP, _I64, _I64, _I64, _I64, _I64, _I32, _P]),
+    ("h3b_a2a_inv_p2p", _I32, [_P, _I64, _PP, ctypes.POINTER(ctypes.c_int64), _I64, _I64, _I64, _I32, _P]),
 ]
 
 
@@ -59,7 +59,7 @@ def _load():
         f = getattr(L, name)
         f.restype = res
         f.argtypes = args
-    if L.h3b_abi_version() != 1:
+    if L.h3b_abi_version() != 2:
         raise ImportError("libh3b.so ABI version mismatch; rebuild it")
     return L
 

@@ -120,8 +120,12 @@ def sdpa_heads(q, k, v):
     return o.squeeze(0).transpose(0, 1).reshape(sq, h * dh)
 
 
-def self_attention(cfg, p, hq, ctx):
-    """hq: the quantised block input (codes, scales) of the modulated h."""
+def self_attention(cfg, p, hq, ctx, overlap_groups=None):
+    """hq: the quantised block input (codes, scales) of the modulated h.
+
+    overlap_groups: head groups of the exchange/attention overlap
+    (sp.sp_attention_overlap, sp_forward.py:299-306); None reads the
+    environment (sp.overlap_groups), 0 or 1 disables it."""
     s = hq[0].shape[0]
     D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
     qkv = _lin_q(hq, p.qkv)  # [s, 3D]
@@ -130,6 +134,10 @@ def self_attention(cfg, p, hq, ctx):
     v = qkv[:, 2 * D:].view(s, H, Dh)
     if ctx is None or ctx.world == 1:
         return _lin(sdpa_heads(q, k, v), p.out)
+    hp = H // ctx.world
+    n = sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups
+    if n > 1 and hp % n == 0:
+        return _lin(sp.sp_attention_overlap(q, k, v, ctx, sdpa_heads, n), p.out)
     q, k, v = sp.a2a_gather_qkv(q, k, v, ctx)  # [S, H/P, Dh] each
     o = sdpa_heads(q, k, v)  # [S, (H/P)*Dh]
     o = sp.a2a_scatter_seq_gather_heads(o, ctx)  # [s_local, D]
@@ -155,7 +163,7 @@ def cross_attention(cfg, p, hq, text):
 FUSED_PRODUCERS = False
 
 
-def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None):
+def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, overlap_groups=None):
     """One fused DiT block on the rank's rows x [s_local, D] (updated in place and returned)."""
     fused = FUSED_PRODUCERS if fused_producers is None else fused_producers
     s1a, sha, ga, s1m, shm, gm = p.tables
@@ -163,7 +171,7 @@ def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None):
         hq = fuse.norm_mod_quant(x, p.n1w, cfg.eps, ridx, s1a, sha)
     else:
         hq = _quant(fuse.norm_mod(x, p.n1w, cfg.eps, ridx, s1a, sha))
-    o = self_attention(cfg, p, hq, ctx)
+    o = self_attention(cfg, p, hq, ctx, overlap_groups)
     if text is not None:
         o = o + cross_attention(cfg, p, hq, text)
     del hq

@@ -5,6 +5,8 @@ Mirrors comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:
   _seq_gather / _seq_scatter                :158-176  (the exchange)
   a2a_gather_seq_scatter_heads(t, ctx)      :179-188  [s_local, H, D] -> [S, H/P, D]
   a2a_scatter_seq_gather_heads(t, ctx)      :191-198  [S, (H/P)*D] -> [s_local, H*D]
+  sp_attention_overlap(q, k, v, ctx, ...)   :211-261  exchange/attention overlap by head groups
+  overlap_groups(hp, world)                 :58,264-273
 and the known-answer start-up probe of sp_group.py:107-128.
 
 Two exchange back ends, chosen per SPContext (`ctx.exchange`):
@@ -77,30 +79,49 @@ def _rows(t):
     return t2, t2.stride(0)
 
 
-def pack(t, world):
-    """[s_local, P*chunk] (rows may be strided) -> [P, s_local, chunk] with the pack kernel."""
+def pack(t, world, width=None, block=None):
+    """[s_local, P*chunk] (rows may be strided) -> [P, s_local, chunk] with the pack kernel.
+
+    With width/block (elements): rows hold one block of `block` elements per
+    rank and the first `width` of each go out (t already offset to the head
+    group's first column; send is [P, s_local, width])."""
     require_cuda(t)
-    t2, ld = _rows(t)
-    s_local, row_elems = t2.shape
-    if row_elems % world:
-        raise ValueError("pack: the row does not split into world chunks")
-    chunk = row_elems // world
-    send = torch.empty((world, s_local, chunk), dtype=t.dtype, device=t.device)
+    if width is None:
+        t2, ld = _rows(t)
+        s_local, row_elems = t2.shape
+        if row_elems % world:
+            raise ValueError("pack: the row does not split into world chunks")
+        width = block = row_elems // world
+    else:
+        t2, ld = t, t.stride(0)
+        s_local = t.shape[0]
+        if t.stride(-1) != 1 or width > block or (world - 1) * block + width > t.shape[1]:
+            raise ValueError("pack: the group does not fit the row")
+    send = torch.empty((world, s_local, width), dtype=t.dtype, device=t.device)
     es = t.element_size()
-    with span("a2a_pack", 2 * s_local * row_elems * es):
-        check(lib.h3b_a2a_pack(ptr(t2), ld * es, ptr(send), s_local, chunk * es, world, stream_of(t)), "h3b_a2a_pack")
+    with span("a2a_pack", 2 * s_local * world * width * es):
+        check(lib.h3b_a2a_pack(ptr(t2), ld * es, ptr(send), s_local, width * es, block * es, world, stream_of(t)),
+              "h3b_a2a_pack")
     return send
 
 
-def unpack(recv):
-    """[P, s_local, chunk] -> [s_local, P*chunk] with the unpack kernel."""
+def unpack(recv, out=None, block=None):
+    """[P, s_local, chunk] -> [s_local, P*chunk] with the unpack kernel.
+
+    With out/block: rank j's chunk of row s lands at column j*block of `out`
+    (a view offset to the head group's first column, unit column stride)."""
     require_cuda(recv)
     world, s_local, chunk = recv.shape
     recv = recv.contiguous()
-    out = torch.empty((s_local, world * chunk), dtype=recv.dtype, device=recv.device)
-    with span("a2a_unpack", 2 * recv.numel() * recv.element_size()):
-        check(lib.h3b_a2a_unpack(ptr(recv), ptr(out), s_local, chunk * recv.element_size(), world, stream_of(recv)),
-              "h3b_a2a_unpack")
+    if out is None:
+        out = torch.empty((s_local, world * chunk), dtype=recv.dtype, device=recv.device)
+        block = chunk
+    elif out.stride(-1) != 1 or out.shape[0] != s_local or chunk > block:
+        raise ValueError("unpack: out does not match recv")
+    es = recv.element_size()
+    with span("a2a_unpack", 2 * recv.numel() * es):
+        check(lib.h3b_a2a_unpack(ptr(recv), ptr(out), out.stride(0) * es, s_local, chunk * es, block * es, world,
+                                 stream_of(recv)), "h3b_a2a_unpack")
     return out
 
 
@@ -144,6 +165,70 @@ def a2a_scatter_seq_gather_heads(t, ctx):
     return unpack(out.view(ctx.world, ctx.local, chunk))
 
 
+def overlap_groups(hp, world):
+    """Number of head groups for the exchange/attention overlap (sp_forward.py:58,264-273).
+
+    H3B_SP_OVERLAP_GROUPS, else the reference's MINIMAX_SP_OVERLAP_CHUNKS (0 or
+    1: no overlap).  At world 4 MINIMAX_SP_OVERLAP_CHUNKS_W4 takes precedence and
+    the count is lowered to the largest divisor of hp not above it, as in the
+    reference.  Every rank must see the same value."""
+    def env(name):
+        return int(os.environ.get(name, "0") or 0)
+    n = env("H3B_SP_OVERLAP_GROUPS") or env("MINIMAX_SP_OVERLAP_CHUNKS")
+    if world == 4:
+        n = env("MINIMAX_SP_OVERLAP_CHUNKS_W4") or n
+        while n > 1 and hp % n:
+            n -= 1
+    return n
+
+
+def sp_attention_overlap(q, k, v, ctx, attn, groups):
+    """Exchange/attention overlap by head groups (sp_forward.py:211-261).
+
+    q, k, v [s_local, H, Dh] (any row stride) -> [s_local, H*Dh].  The H/P heads
+    a rank receives are split into `groups` groups of hc heads; group g's forward
+    exchange (the hc heads j*hp + g*hc .. of every destination rank j), its
+    attention `attn(q_g, k_g, v_g)` ([S, hc, Dh] each -> [S, hc*Dh]) and its
+    inverse exchange are pipelined, so group g+1's transfer runs during group
+    g's attention.  Each head is computed exactly as without the overlap, so
+    the result is identical."""
+    s_local, heads, dim = q.shape
+    hp = heads // ctx.world
+    if groups < 1 or hp % groups:
+        raise ValueError(f"{groups} groups do not divide the {hp} heads of a rank")
+    if ctx.exchange == "p2p":
+        return ctx.peer.attention_overlap(q, k, v, ctx, attn, groups)
+    P, hc = ctx.world, hp // groups
+    w = hc * dim
+    pending = []
+    keep = []  # send/receive tensors of collectives still in flight
+    for g in range(groups):
+        trio = []
+        for t in (q, k, v):
+            t2, _ = _rows(t)
+            send = pack(t2[:, g * w:], P, width=w, block=hp * dim)
+            recv = torch.empty(ctx.seq_len * w, dtype=t.dtype, device=t.device)
+            trio.append((recv, _seq_gather(recv, send.view(-1), ctx, w, async_op=True)))
+            keep.append(send)
+        pending.append(trio)
+    final = torch.empty(s_local, heads * dim, dtype=q.dtype, device=q.device)
+    outs = []
+    for g in range(groups):
+        parts = []
+        for recv, work in pending[g]:
+            work.wait()
+            parts.append(recv.view(ctx.seq_len, hc, dim))
+        o = attn(*parts).contiguous()
+        ob = torch.empty(P * s_local * w, dtype=o.dtype, device=o.device)
+        outs.append((g, ob, _seq_scatter(ob, o.view(-1), ctx, w, async_op=True)))
+        keep.append(o)
+    for g, ob, work in outs:
+        work.wait()
+        unpack(ob.view(P, s_local, w), out=final[:, g * w:], block=hp * dim)
+    del keep
+    return final
+
+
 # ---------------------------------------------------------------------------
 # Peer-memory back end
 
@@ -173,6 +258,7 @@ class PeerExchange:
         self.out = torch.empty((max_local, world * self.chunk), dtype=dtype, device=dev)
         self.flags = torch.zeros(world, dtype=torch.int32, device=dev)
         self.epoch = 0
+        self.comm = None  # side stream of the exchange/attention overlap
         self._bases = []
         mine = [self._handle(t) for t in self.recv + [self.out, self.flags]]
         gathered = [None] * world
@@ -216,8 +302,24 @@ class PeerExchange:
                                        stream_of(stream_tensor)), "h3b_peer_barrier")
         del keep
 
-    def fwd(self, tensors, ctx):
-        """tensors: n x [s_local, H, D] -> n views [S, H/P, D] of the receive buffers."""
+    def _group(self, groups):
+        """(width in elements, hc) of one of `groups` head groups of a rank's chunk."""
+        hp = self.heads // self.world
+        if groups < 1 or hp % groups:
+            raise ValueError(f"{groups} groups do not divide the {hp} heads of a rank")
+        return self.chunk // groups, hp // groups
+
+    def recv_views(self, n, ctx, g=0, groups=1):
+        """Views [S, hc, Dh] of head group g in the first n receive buffers.  Group
+        g of width w occupies elements [g*seq_len*w, (g+1)*seq_len*w) of a buffer."""
+        w, hc = self._group(groups)
+        base = g * self.seq_len * w
+        return [self.recv[i].view(-1)[base: base + ctx.seq_len * w].view(ctx.seq_len, hc, self.head_dim)
+                for i in range(n)]
+
+    def fwd_copy(self, tensors, ctx, g=0, groups=1):
+        """Store head group g of this rank's rows of each tensor into every rank's
+        receive buffers (no barrier: the caller brackets it)."""
         n = len(tensors)
         if n > len(self.recv):
             raise ValueError("more tensors than receive buffers")
@@ -235,33 +337,81 @@ class PeerExchange:
             if t.dtype != self.dtype or t.shape != srcs[0].shape:
                 raise ValueError("all tensors must share shape and dtype")
         es = srcs[0].element_size()
+        w, _ = self._group(groups)
+        base = g * self.seq_len * w * es
         src_arr, k1 = ptr_array([t.data_ptr() for t in srcs])
-        dst_arr, k2 = ptr_array([self.peer_recv[i][j] for i in range(n) for j in range(self.world)])
-        self.barrier(srcs[0])
-        off_rank = n * s_local * self.chunk * es * (self.world - 1)
+        dst_arr, k2 = ptr_array([self.peer_recv[i][j] + base for i in range(n) for j in range(self.world)])
+        off_rank = n * s_local * w * es * (self.world - 1)
         with span("a2a_fwd_p2p", off_rank):
-            check(lib.h3b_a2a_fwd_p2p(n, src_arr, ld * es, dst_arr, s_local, ctx.start, self.chunk * es, self.world,
-                                      stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
-        self.barrier(srcs[0])
+            check(lib.h3b_a2a_fwd_p2p(n, src_arr, ld * es, dst_arr, s_local, ctx.start, w * es, self.chunk * es,
+                                      g * w * es, self.world, stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
         del k1, k2
-        hp = heads // self.world
-        return [self.recv[i][: ctx.seq_len].view(ctx.seq_len, hp, dim) for i in range(n)]
+
+    def fwd(self, tensors, ctx):
+        """tensors: n x [s_local, H, D] -> n views [S, H/P, D] of the receive buffers."""
+        self.barrier(tensors[0])
+        self.fwd_copy(tensors, ctx)
+        self.barrier(tensors[0])
+        return self.recv_views(len(tensors), ctx)
+
+    def inv_copy(self, t, ctx, g=0, groups=1):
+        """Store t [S, w] (head group g of this rank's heads, unit column stride)
+        into every rank's output buffer (no barrier: the caller brackets it)."""
+        require_cuda(t)
+        w, _ = self._group(groups)
+        if t.dim() != 2 or t.shape[1] != w or t.stride(1) != 1 or t.dtype != self.dtype:
+            raise ValueError("inv: t must be [S, width] with unit column stride")
+        es = t.element_size()
+        dst_arr, k1 = ptr_array(self.peer_out)
+        splits = (ctypes.c_int64 * self.world)(*ctx.splits)
+        off_rank = (ctx.seq_len - ctx.local) * w * es
+        with span("a2a_inv_p2p", off_rank):
+            check(lib.h3b_a2a_inv_p2p(ptr(t), t.stride(0) * es, dst_arr, splits, w * es, self.world * self.chunk * es,
+                                      (self.rank * self.chunk + g * w) * es, self.world, stream_of(t)),
+                  "h3b_a2a_inv_p2p")
+        del k1
 
     def inv(self, t, ctx):
         """t [S, (H/P)*D] (unit stride along the row) -> [s_local, H*D] view of the output buffer."""
-        require_cuda(t)
-        if t.dim() != 2 or t.shape[1] != self.chunk or t.stride(1) != 1 or t.dtype != self.dtype:
-            raise ValueError("inv: t must be [S, chunk] with unit column stride")
-        dst_arr, k1 = ptr_array(self.peer_out)
-        splits = (ctypes.c_int64 * self.world)(*ctx.splits)
         self.barrier(t)
-        off_rank = (ctx.seq_len - ctx.local) * self.chunk * t.element_size()
-        with span("a2a_inv_p2p", off_rank):
-            check(lib.h3b_a2a_inv_p2p(ptr(t), t.stride(0) * t.element_size(), dst_arr, splits,
-                                      self.chunk * t.element_size(), self.world, self.rank, stream_of(t)),
-                  "h3b_a2a_inv_p2p")
+        self.inv_copy(t, ctx)
         self.barrier(t)
-        del k1
+        return self.out[: ctx.local]
+
+    def attention_overlap(self, q, k, v, ctx, attn, groups):
+        """sp_attention_overlap over peer memory.  The exchanges run on a
+        high-priority side stream: one barrier (every rank's receive and output
+        buffers are free: each rank's previous readers of them precede its
+        arrival), then per group a copy and a barrier (group g has arrived
+        everywhere); the attention of group g waits for that, and its inverse
+        copy waits for the attention.  One last barrier: every rank's output
+        buffer is complete.  Returns [s_local, H*D], a view of the output buffer."""
+        cur = torch.cuda.current_stream(q.device)
+        if self.comm is None:
+            self.comm = torch.cuda.Stream(device=q.device, priority=-100)
+        comm = self.comm
+        comm.wait_stream(cur)
+        arrived = []
+        with torch.cuda.stream(comm):
+            self.barrier(q)
+            for g in range(groups):
+                self.fwd_copy([q, k, v], ctx, g, groups)
+                self.barrier(q)
+                ev = torch.cuda.Event()
+                ev.record(comm)
+                arrived.append(ev)
+        keep = []  # attention outputs read by the side stream until it is joined
+        for g in range(groups):
+            cur.wait_event(arrived[g])
+            o = attn(*self.recv_views(3, ctx, g, groups))
+            keep.append(o)
+            comm.wait_stream(cur)
+            with torch.cuda.stream(comm):
+                self.inv_copy(o, ctx, g, groups)
+        with torch.cuda.stream(comm):
+            self.barrier(q)
+        cur.wait_stream(comm)
+        del keep
         return self.out[: ctx.local]
 
     def close(self):

@@ -4,6 +4,7 @@ Follows comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py of the reference:
   SPContext splits / start / stop        :140-155
   forward pack + exchange (+no unpack)   :158-166, :179-188
   inverse exchange + unpack              :169-176, :191-198
+  head-group pack of the overlap         :222-224
 and the NCCL start-up known-answer test of sp_group.py:107-124.
 The exchange of all ranks is simulated in one process: `sends[r]` is what rank
 r hands to all_to_all_single and the function returns what every rank receives.
@@ -28,6 +29,15 @@ def pack_fwd(t, world):
     s_local, heads, dim = t.shape
     hp = heads // world
     return np.ascontiguousarray(t.reshape(s_local, world, hp * dim).transpose(1, 0, 2))
+
+
+def pack_group(t, world, groups, g):
+    """Head group g of every destination's heads: [s_local, H, Dh] -> send
+    [P, s_local, hc*Dh], hc = H/P/groups (prep() of sp_attention_overlap,
+    sp_forward.py:222-224)."""
+    s_local, heads, dim = t.shape
+    w = heads // world // groups * dim
+    return np.ascontiguousarray(t.reshape(s_local, world, groups, w)[:, :, g].transpose(1, 0, 2))
 
 
 def a2a_fwd(ts, world):

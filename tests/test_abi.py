@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     for n in declared():
         assert hasattr(L, n)
     L.h3b_abi_version.restype = ctypes.c_int
-    assert L.h3b_abi_version() == 1
+    assert L.h3b_abi_version() == 2
 
 
 def test_every_declaration_cites_a_reference_interface():

@@ -2,7 +2,8 @@
 
 Covers the parts of the Ulysses path that are not kernels: SPContext's row
 splits, the exchange calls with their split sizes (h3b.sp._seq_gather /
-_seq_scatter, fed with oracle-packed buffers), the start-up known-answer probe,
+_seq_scatter, fed with oracle-packed buffers; whole and per head group), the
+start-up known-answer probe,
 and failure detection -- a rank that never reaches the exchange makes the other
 rank's collective fail within the process-group timeout instead of hanging.
 """
@@ -68,6 +69,23 @@ def _worker_exchange(rank, world, port, S, q):
         sp._seq_scatter(recv, torch.from_numpy(obits[rank].view(np.float16)).reshape(-1), ctx, hp * Dh)
         got = sp_layout.unpack_inv(recv.numpy().view(np.uint16).reshape(world, ctx.local, hp * Dh), world)
         np.testing.assert_array_equal(got, sp_layout.a2a_inv(obits, world)[rank])
+        # head groups of the exchange/attention overlap (sp_forward.py:211-261):
+        # per group the exchange moves hc*Dh-wide rows; the groups reassemble both ways
+        groups = 2
+        w = hp // groups * Dh
+        for g in range(groups):
+            send = torch.from_numpy(sp_layout.pack_group(bits[rank], world, groups, g).view(np.float16)).reshape(-1)
+            out = torch.empty(S * w, dtype=torch.float16)
+            sp._seq_gather(out, send, ctx, w)
+            np.testing.assert_array_equal(out.numpy().view(np.uint16).reshape(S, w),
+                                          ref.reshape(S, hp * Dh)[:, g * w:(g + 1) * w])
+        final = np.zeros((ctx.local, world, groups, w), np.uint16)
+        for g in range(groups):
+            recv = torch.empty(world * ctx.local * w, dtype=torch.float16)
+            part = np.ascontiguousarray(obits[rank][:, g * w:(g + 1) * w])
+            sp._seq_scatter(recv, torch.from_numpy(part.view(np.float16)).reshape(-1), ctx, w)
+            final[:, :, g] = recv.numpy().view(np.uint16).reshape(world, ctx.local, w).transpose(1, 0, 2)
+        np.testing.assert_array_equal(final.reshape(ctx.local, -1), sp_layout.a2a_inv(obits, world)[rank])
         sp.startup_probe(rank, world, dist.group.WORLD, torch.device("cpu"))
         dist.barrier()
         dist.destroy_process_group()
@@ -131,3 +149,21 @@ def test_dead_peer_fails_within_timeout():
     r0 = res.get(0)
     assert isinstance(r0, tuple) and r0[0] == "raised", res
     assert r0[1] < 60, f"the surviving rank waited {r0[1]:.1f} s"
+
+
+def test_overlap_groups_env(monkeypatch):
+    """Group count of the exchange/attention overlap from the environment
+    (sp_forward.py:58,264-273): off by default; at world 4 the count drops to a
+    divisor of the rank's heads and the _W4 variable takes precedence."""
+    sys.path.insert(0, os.path.join(ROOT, "minimax-h3-multi-dgx-spark_b200"))
+    from h3b import sp
+    for k in ("H3B_SP_OVERLAP_GROUPS", "MINIMAX_SP_OVERLAP_CHUNKS", "MINIMAX_SP_OVERLAP_CHUNKS_W4"):
+        monkeypatch.delenv(k, raising=False)
+    assert sp.overlap_groups(20, 2) == 0
+    monkeypatch.setenv("MINIMAX_SP_OVERLAP_CHUNKS", "4")
+    assert sp.overlap_groups(20, 2) == 4
+    assert sp.overlap_groups(10, 4) == 2  # 4 does not divide 10 -> 2
+    monkeypatch.setenv("MINIMAX_SP_OVERLAP_CHUNKS_W4", "5")
+    assert sp.overlap_groups(10, 4) == 5
+    monkeypatch.setenv("H3B_SP_OVERLAP_GROUPS", "5")
+    assert sp.overlap_groups(5, 8) == 5

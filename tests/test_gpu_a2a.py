@@ -50,6 +50,20 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+def _fwd_p2p(n, srcs, src_ld, dsts, s_local, row_start, width, block, offset, world):
+    src, k1 = ptr_array([t.data_ptr() for t in srcs])
+    dst, k2 = ptr_array(dsts)
+    check(lib.h3b_a2a_fwd_p2p(n, src, src_ld, dst, s_local, row_start, width, block, offset, world, _stream()),
+          "fwd_p2p")
+
+
+def _inv_p2p(src, dsts, splits, width, dst_ld, offset, world):
+    dst, k = ptr_array(dsts)
+    sp = (ctypes.c_int64 * world)(*splits)
+    check(lib.h3b_a2a_inv_p2p(ctypes.c_void_p(src.data_ptr()), src.stride(0) * 2, dst, sp, width, dst_ld, offset,
+                              world, _stream()), "inv_p2p")
+
+
 @pytest.mark.parametrize("world,S", [(2, 1001), (4, 4130), (8, 8192)])
 def test_p2p_kernels_emulated(world, S):
     """Every rank's fwd/inv launch on one GPU against sp_layout.a2a_fwd / a2a_inv."""
@@ -64,10 +78,8 @@ def test_p2p_kernels_emulated(world, S):
     qd = [q.to(DEV) for q in qs]
     kd = [k.to(DEV) for k in ks]
     for r in range(world):
-        src, k1 = ptr_array([qd[r].data_ptr(), kd[r].data_ptr()])
-        dst, k2 = ptr_array([t.data_ptr() for t in recv_q] + [t.data_ptr() for t in recv_k])
-        check(lib.h3b_a2a_fwd_p2p(2, src, H * DH * 2, dst, splits[r], starts[r], chunk * 2, world, _stream()),
-              "fwd_p2p")
+        _fwd_p2p(2, [qd[r], kd[r]], H * DH * 2, [t.data_ptr() for t in recv_q] + [t.data_ptr() for t in recv_k],
+                 splits[r], starts[r], chunk * 2, chunk * 2, 0, world)
     torch.cuda.synchronize()
     ref_q = sp_layout.a2a_fwd([bits(q) for q in qs], world)
     ref_k = sp_layout.a2a_fwd([bits(k) for k in ks], world)
@@ -78,15 +90,66 @@ def test_p2p_kernels_emulated(world, S):
     outs = [randn_bf16((S, chunk + 64), seed=3000 + j) for j in range(world)]
     od = [o.to(DEV)[:, :chunk] for o in outs]
     res = [torch.empty(splits[r], world * chunk, dtype=torch.bfloat16, device=DEV) for r in range(world)]
-    sp = (ctypes.c_int64 * world)(*splits)
     for j in range(world):
-        dst, k3 = ptr_array([t.data_ptr() for t in res])
-        check(lib.h3b_a2a_inv_p2p(ctypes.c_void_p(od[j].data_ptr()), od[j].stride(0) * 2, dst, sp, chunk * 2, world, j,
-                                  _stream()), "inv_p2p")
+        _inv_p2p(od[j], [t.data_ptr() for t in res], splits, chunk * 2, world * chunk * 2, j * chunk * 2, world)
     torch.cuda.synchronize()
     ref = sp_layout.a2a_inv([bits(o)[:, :chunk] for o in outs], world)
     for r in range(world):
         np.testing.assert_array_equal(bits(res[r]), ref[r])
+
+
+@pytest.mark.parametrize("world,S,groups", [(2, 1001, 4), (4, 4130, 2), (8, 8192, 5), (2, 999, 20)])
+def test_p2p_head_groups_emulated(world, S, groups):
+    """Head-group exchanges (the overlap's per-group copies): group g of every
+    destination rank's heads lands in that group's region of the receive buffer,
+    and the per-group inverse copies assemble the same output as one exchange."""
+    splits = sp_layout.splits(S, world)
+    starts = sp_layout.starts(S, world)
+    hp = H // world
+    hc = hp // groups
+    chunk, w = hp * DH, hc * DH
+    qkv = [randn_bf16((splits[r], 3 * H * DH), seed=4000 + r) for r in range(world)]
+    qkv_d = [t.to(DEV) for t in qkv]
+    recv = [[torch.empty(S * chunk, dtype=torch.bfloat16, device=DEV) for _ in range(world)] for _ in range(3)]
+    for g in range(groups):
+        for r in range(world):
+            srcs = [qkv_d[r][:, i * H * DH:] for i in range(3)]
+            dsts = [recv[i][j].data_ptr() + g * S * w * 2 for i in range(3) for j in range(world)]
+            _fwd_p2p(3, srcs, 3 * H * DH * 2, dsts, splits[r], starts[r], w * 2, chunk * 2, g * w * 2, world)
+    torch.cuda.synchronize()
+    for i in range(3):
+        ref = sp_layout.a2a_fwd([bits(t)[:, i * H * DH:(i + 1) * H * DH].reshape(-1, H, DH) for t in qkv], world)
+        for j in range(world):
+            got = bits(recv[i][j]).reshape(groups, S, hc, DH)
+            for g in range(groups):
+                np.testing.assert_array_equal(got[g], ref[j][:, g * hc:(g + 1) * hc])
+    outs = [[randn_bf16((S, w), seed=5000 + 37 * j + g) for g in range(groups)] for j in range(world)]
+    res = [torch.empty(splits[r], world * chunk, dtype=torch.bfloat16, device=DEV) for r in range(world)]
+    for g in range(groups):
+        for j in range(world):
+            _inv_p2p(outs[j][g].to(DEV), [t.data_ptr() for t in res], splits, w * 2, world * chunk * 2,
+                     (j * chunk + g * w) * 2, world)
+    torch.cuda.synchronize()
+    ref = sp_layout.a2a_inv([np.concatenate([bits(o) for o in outs[j]], axis=1) for j in range(world)], world)
+    for r in range(world):
+        np.testing.assert_array_equal(bits(res[r]), ref[r])
+
+
+@pytest.mark.parametrize("world,s_local,groups", [(2, 1000, 4), (8, 777, 5), (4, 64, 10)])
+def test_pack_unpack_head_groups(world, s_local, groups):
+    """Group pack/unpack of the NCCL overlap path against numpy slicing."""
+    hp = H // world
+    hc = hp // groups
+    w = hc * DH
+    qkv = randn_bf16((s_local, 3 * H * DH), seed=world + s_local)
+    k = qkv.to(DEV)[:, H * DH:2 * H * DH]
+    kb = bits(qkv)[:, H * DH:2 * H * DH].reshape(s_local, world, groups, w)
+    final = torch.zeros(s_local, H * DH, dtype=torch.bfloat16, device=DEV)
+    for g in range(groups):
+        send = h3b.pack(k[:, g * w:], world, width=w, block=hp * DH)
+        np.testing.assert_array_equal(bits(send), kb[:, :, g].transpose(1, 0, 2))
+        h3b.unpack(send, out=final[:, g * w:], block=hp * DH)
+    np.testing.assert_array_equal(bits(final), bits(qkv)[:, H * DH:2 * H * DH])
 
 
 def test_peer_barrier_times_out_and_reports():

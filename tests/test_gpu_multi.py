@@ -9,8 +9,10 @@ restatement locally.  Checked bit-exactly:
     all_to_all_single, unpack kernel) and peer-memory back end (fused p2p
     kernels + flag barriers), with an uneven row split;
   * the same exchanges done the reference's way (reshape + all_to_all_single);
-  * one full DiT block (p2p exchange) against the eager PyTorch
-    block using all_to_all_single.
+  * the exchange/attention overlap by head groups (both back ends, several
+    group counts) against the plain exchange;
+  * one full DiT block (p2p exchange, with and without the overlap) against
+    the eager PyTorch block using all_to_all_single.
 """
 import os
 import socket
@@ -78,6 +80,18 @@ def _worker(rank, world, port, q):
                         np.testing.assert_array_equal(_bits(got[i]), ref_fwd[i], err_msg=f"{exch} fwd S={S} t={i}")
                     inv = h3b.a2a_scatter_seq_gather_heads(o_mine, ctx)
                     np.testing.assert_array_equal(_bits(inv), ref_inv, err_msg=f"{exch} inv S={S}")
+            # exchange/attention overlap by head groups (sp_forward.py:211-261); the
+            # routing is checked with an elementwise stand-in for attention
+            def mix(a, b, c):
+                return (a * 3 + b - c).reshape(a.shape[0], -1)
+            ctx_n = h3b.SPContext(rank, world, g, S)
+            o_ref = _bits(h3b.a2a_scatter_seq_gather_heads(mix(*h3b.a2a_gather_qkv(*mine, ctx_n)), ctx_n))
+            for exch in ("nccl", "p2p"):
+                ctx = h3b.SPContext(rank, world, g, S, exchange=exch, peer=peer if exch == "p2p" else None)
+                for groups in sorted({n for n in (2, 5, hp) if n > 1 and hp % n == 0}):
+                    for rep in range(2):
+                        got = h3b.sp_attention_overlap(*mine, ctx, mix, groups)
+                        np.testing.assert_array_equal(_bits(got), o_ref, err_msg=f"{exch} overlap {groups} S={S}")
             # the reference's own formulation
             ctx = h3b.SPContext(rank, world, g, S)
             np.testing.assert_array_equal(_bits(tp.a2a_gather_seq_scatter_heads(mine[0], ctx)), ref_fwd[0])
@@ -100,6 +114,11 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize(dev)
         bad = (y.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
         assert bad == 0, f"block at world {world}: {bad} elements differ"
+        # the same block with the exchange/attention overlap (one head per group)
+        y2 = hm.block_forward(cfg, p, x.clone(), ridx, ctx, overlap_groups=cfg.heads // world)
+        torch.cuda.synchronize(dev)
+        bad = (y2.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
+        assert bad == 0, f"overlapped block at world {world}: {bad} elements differ"
         assert h3b.status() == 0
         dist.barrier(device_ids=[rank])
         peer.close()
