@@ -3,6 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload dit_block|dit_step|linear|fused|a2a] [--seq S] [--exchange p2p|nccl]
+                    [--overlap G]
 
 Default workload (dit_block): one synthetic DiT block of the benchmark's
 block configuration -- D=5120, 40 heads x 128, FFN 13824 (GELU-tanh), four
@@ -16,7 +17,10 @@ events on the compute stream, max over ranks.  Inputs (x 1.31 GB/N, weights
 
 Prints ONE JSON line on rank 0.  `value` is ms per step (lower is better);
 `e2e` repeats the step through host buffers (pinned H2D of the step's input
-rows and conditioning, D2H of the output rows); `roofline` is the INT8 GEMM
+rows and conditioning, D2H of the output rows, every step inside the timed
+region) with h3b.model.HostPipeline, whose copy streams move step k+1's input
+and step k-1's output during step k; `e2e.serial_ms_per_step` is the same with
+copies and compute in sequence on one stream; `roofline` is the INT8 GEMM
 (the dominant kernel of this library) timed by CUDA events inside the timed
 region; `cpu_baseline` times the reference's eager PyTorch path on the host's
 cores on a bounded sample of the same workload (rank 0, N=1 only).
@@ -168,9 +172,11 @@ def max_over_ranks(v, world, dev):
     return float(t.item())
 
 
-def timed(step, steps, warmup, world, dev, sample_clocks=True):
+def timed(step, steps, warmup, world, dev, sample_clocks=True, finish=None):
     for _ in range(warmup):
         step()
+    if finish is not None:
+        finish()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier(device_ids=[dev.index])
@@ -183,6 +189,8 @@ def timed(step, steps, warmup, world, dev, sample_clocks=True):
     e0.record()
     for _ in range(steps):
         step()
+    if finish is not None:
+        finish()  # e.g. join side streams, so e1 follows all of the steps' work
     e1.record()
     torch.cuda.synchronize(dev)
     if sampler:
@@ -264,21 +272,39 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
 
     e2e = None
     if not args.no_e2e:
-        out_host = torch.empty_like(x_host).pin_memory()
         e_host = [p.e.detach().cpu().pin_memory() for p in dit.params]
 
-        def step_e2e():
+        def load_tables():
             for p, eh in zip(dit.params, e_host):
                 p.e.copy_(eh, non_blocking=True)
                 p.tables = h3b.modulation_tables(*(p.e[:, i] for i in range(6)))
+
+        # pipelined: HostPipeline, input copy of step k+1 / output copy of step
+        # k-1 on copy streams during step k (three device slots)
+        pipe = hm.HostPipeline(dit, s_local, ridx, ctx, text, depth=3)
+        outs = [torch.empty_like(x_host).pin_memory() for _ in range(3)]
+
+        def step_pipe():
+            pipe.submit(x_host, outs[pipe.k % 3], before=load_tables)
+
+        ms_e2e, _ = timed(step_pipe, args.steps, 1, world, dev, sample_clocks=False, finish=pipe.flush)
+        del pipe
+        # serial: copy in, forward, copy out, all on the compute stream
+        out_host = outs[0]
+
+        def step_serial():
+            load_tables()
             xw.copy_(x_host, non_blocking=True)
             y = dit.forward(xw, ridx, ctx, text)
             out_host.copy_(y, non_blocking=True)
 
-        ms_e2e, _ = timed(step_e2e, args.steps, 1, world, dev, sample_clocks=False)
+        ms_serial, _ = timed(step_serial, args.steps, 1, world, dev, sample_clocks=False)
         h2d = x_host.numel() * 2 + sum(e.numel() * 2 for e in e_host)
         e2e = {"value": round(ms_e2e, 3), "unit": "ms/step", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": out_host.numel() * 2}
+               "d2h_bytes_per_step": out_host.numel() * 2,
+               "api": "h3b.model.HostPipeline.submit (pinned host latents in and out; copies on two copy streams "
+                      "overlap the neighbouring steps' compute, every step's copies inside the timed region)",
+               "serial_ms_per_step": round(ms_serial, 3)}
     status = h3b.status()
     if status:
         raise RuntimeError(f"device status {status} after the timed region")

@@ -22,6 +22,10 @@ output before the gated residual, so the fused norm chain is unchanged and no
 exchange is needed for it.  The reference model has no such branch in this
 file set; the layout is this harness's choice.
 
+HostPipeline runs host-resident latents through the model with the input and
+output copies on their own streams, overlapping the previous and next steps'
+copies with each step's compute.
+
 Weights are int8 with per-output-channel fp32 scales and bf16 biases, drawn
 from a seeded generator on the target device.  Attention stays PyTorch's
 scaled_dot_product_attention, as in the reference.
@@ -202,3 +206,58 @@ class SynthDiT:
         for p in self.params:
             x = block_forward(self.cfg, p, x, ridx, ctx, text)
         return x
+
+
+class HostPipeline:
+    """Host-resident latents through a model, with the copies off the compute stream.
+
+    submit(x_host, out_host) runs one step: the rows x_host [rows, D] (pinned
+    bf16) are copied to the device on an input copy stream, `model.forward`
+    runs on the current stream, and the result is copied into out_host (pinned)
+    on an output copy stream.  Up to `depth` steps are in flight on `depth`
+    device slots, so the input copy of step k+1 and the output copy of step
+    k-1 run during step k's compute; a slot is refilled only after its previous
+    output copy has finished.  flush() makes the current stream wait for every
+    copy issued so far: out_host of a submitted step is valid once the current
+    stream has passed that point (e.g. after flush() and a synchronize).
+    `before` (optional) is called on the current stream before each forward,
+    for per-step device inputs such as the modulation tables."""
+
+    def __init__(self, model, rows, ridx, ctx=None, text=None, depth=3):
+        self.model, self.ridx, self.ctx, self.text = model, ridx, ctx, text
+        dev = model.device
+        self.device = dev
+        self.slots = [torch.empty(rows, model.cfg.dim, dtype=torch.bfloat16, device=dev) for _ in range(depth)]
+        self.freed = [None] * depth
+        self.copy_in = torch.cuda.Stream(device=dev)
+        self.copy_out = torch.cuda.Stream(device=dev)
+        self.k = 0
+
+    def submit(self, x_host, out_host, before=None):
+        i = self.k % len(self.slots)
+        slot = self.slots[i]
+        cur = torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(self.copy_in):
+            if self.freed[i] is not None:
+                self.copy_in.wait_event(self.freed[i])
+            slot.copy_(x_host, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(self.copy_in)
+        cur.wait_event(ready)
+        if before is not None:
+            before()
+        y = self.model.forward(slot, self.ridx, self.ctx, self.text)
+        done = torch.cuda.Event()
+        done.record(cur)
+        self.copy_out.wait_event(done)
+        with torch.cuda.stream(self.copy_out):
+            out_host.copy_(y, non_blocking=True)
+            freed = torch.cuda.Event()
+            freed.record(self.copy_out)
+        self.freed[i] = freed
+        self.k += 1
+
+    def flush(self):
+        cur = torch.cuda.current_stream(self.device)
+        cur.wait_stream(self.copy_in)
+        cur.wait_stream(self.copy_out)
