@@ -92,6 +92,25 @@ H3B_API int h3b_int8_mm_scaled(const int8_t *xq, const int8_t *w, const float *x
 H3B_API int h3b_int8_mm_i32(const int8_t *xq, const int8_t *w, int32_t *acc, int64_t M, int64_t N, int64_t K,
                     void *stream);
 
+/* h3b_int8_mm_scaled fused with the Ulysses forward all-to-all: instead of
+ * out [M,N], the epilogue stores each output column straight into the receive
+ * buffer of the rank that owns its head, over NVLink for the other ranks.
+ * N = S_g * seg_cols (S_g <= 3 segments: q, k, v of a fused qkv projection);
+ * column n belongs to segment t = n / seg_cols and head h = (n % seg_cols) /
+ * head_dim, owned by rank j = h / heads_per_rank; it is stored to
+ * dst[t * world + j] (bf16, rows of heads_per_rank * head_dim elements; at
+ * least row_start + M rows) at row row_start + m, column
+ * (h - j * heads_per_rank) * head_dim + n % head_dim -- exactly what
+ * h3b_a2a_fwd_p2p delivers after an unfused GEMM, value for value.
+ * head_dim % 64 == 0, seg_cols == world * heads_per_rank * head_dim,
+ * world <= 8.  Bracket with h3b_peer_barrier like the exchange it replaces.
+ * Replaces the qkv projection + a2a_gather_seq_scatter_heads (x3) of
+ * sp_attention, comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:284,308-311. */
+H3B_API int h3b_int8_mm_scaled_a2a(const int8_t *xq, const int8_t *w, const float *xs, const float *ws,
+                                   const void *bias, int64_t M, int64_t N, int64_t K, void *const *dst,
+                                   int64_t row_start, int64_t seg_cols, int64_t head_dim, int64_t heads_per_rank,
+                                   int world, void *stream);
+
 /* Patched Linear forward: quantise x (h3b_quant_rowwise) into the caller's
  * scratch xq [M,K] / xs [M], then h3b_int8_mm_scaled into out [M,N].
  * Replaces the patched comfy_kitchen.backends.cuda.int8_linear,

@@ -52,6 +52,21 @@ constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM >> 4) << 24);
 
+constexpr int kMaxScatterSegs = 3;   // q, k, v
+constexpr int kMaxScatterWorld = 8;
+
+// Scatter epilogue: the GEMM fused with the Ulysses forward exchange.  Output
+// column n lies in segment t = n / seg (q, k, v), head h = (n % seg) / head_dim,
+// which rank j = h / hp owns; it is stored into rank j's receive buffer
+// dst[t * world + j] (a peer's memory for j != this rank) at row row_start + m
+// and column (h - j*hp)*head_dim + n % head_dim, receive rows being
+// hp*head_dim elements wide -- the layout the exchange delivers.
+struct Scatter {
+    uint16_t* dst[kMaxScatterSegs * kMaxScatterWorld];
+    int64_t row_start;
+    int seg, head_dim, hp, world;
+};
+
 struct Args {
     const float* xs;
     const float* ws;
@@ -60,6 +75,7 @@ struct Args {
     int M, N, K;
     int* status;
     int tile_n;  // 2-CTA kernel: output tile width (multiple of 32, <= 256)
+    Scatter sc;  // scatter epilogue only
 };
 
 // ---------------------------------------------------------------------------
@@ -166,10 +182,40 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
     nb = r / gsize;
 }
 
+// bf16((float(acc) * xs) * ws[n] [+ bias[n]]) of 8 columns cb .. cb+7 of one
+// row (int32 sums r[0..7]) with separate IEEE products, packed in pairs.
+__device__ __forceinline__ uint4 dequant8(const Args& args, const uint32_t* r, int cb, float xs) {
+    const float4 w0 = *reinterpret_cast<const float4*>(args.ws + cb);
+    const float4 w1 = *reinterpret_cast<const float4*>(args.ws + cb + 4);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (args.bias) {
+        const uint4 b = *reinterpret_cast<const uint4*>(args.bias + cb);
+        const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            bv[2 * e] = bf16_lo(bu[e]);
+            bv[2 * e + 1] = bf16_hi(bu[e]);
+        }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        float v0 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[2 * e]), xs), wv[2 * e]);
+        float v1 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[2 * e + 1]), xs), wv[2 * e + 1]);
+        if (args.bias) {
+            v0 = __fadd_rn(v0, bv[2 * e]);
+            v1 = __fadd_rn(v1, bv[2 * e + 1]);
+        }
+        o[e] = pack_bf16x2(v0, v1);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Dequantise one 32-column chunk of one tile row (registers r) and store it:
-// out[row, col0 .. col0+31] = bf16((float(acc) * xs) * ws[n] [+ bias[n]]) with
-// separate IEEE products, or the raw int32 sums.  N % 8 == 0, so every 8-column
-// group is either fully inside or fully outside the matrix.
+// out[row, col0 .. col0+31] = bf16((float(acc) * xs) * ws[n] [+ bias[n]]), or
+// the raw int32 sums.  N % 8 == 0, so every 8-column group is either fully
+// inside or fully outside the matrix.
 template <bool OUT_I32>
 __device__ __forceinline__ void store_chunk(const Args& args, const uint32_t (&r)[32], int row, int col0, float xs) {
     const int N = args.N;
@@ -184,33 +230,43 @@ __device__ __forceinline__ void store_chunk(const Args& args, const uint32_t (&r
         for (int g = 0; g < 4; ++g) {
             const int cb = col0 + 8 * g;
             if (cb >= N) break;
-            const float4 w0 = *reinterpret_cast<const float4*>(args.ws + cb);
-            const float4 w1 = *reinterpret_cast<const float4*>(args.ws + cb + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            float bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (args.bias) {
-                const uint4 b = *reinterpret_cast<const uint4*>(args.bias + cb);
-                const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    bv[2 * e] = bf16_lo(bu[e]);
-                    bv[2 * e + 1] = bf16_hi(bu[e]);
-                }
-            }
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float v0 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e]), xs), wv[2 * e]);
-                float v1 = __fmul_rn(__fmul_rn(__int2float_rn((int)r[8 * g + 2 * e + 1]), xs), wv[2 * e + 1]);
-                if (args.bias) {
-                    v0 = __fadd_rn(v0, bv[2 * e]);
-                    v1 = __fadd_rn(v1, bv[2 * e + 1]);
-                }
-                o[e] = pack_bf16x2(v0, v1);
-            }
-            dst[g] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[g] = dequant8(args, r + 8 * g, cb, xs);
         }
     }
+}
+
+// Scatter epilogue of one 64-column unit of the 32 tile rows row0 .. row0+31
+// held by this warp (lane = row): dequantise into the warp's 4 KB staging
+// area (row-major 32 x 128 B, 16-byte pieces XOR-swizzled by row so that both
+// the row-wise writes and the piece-wise reads are conflict-free), then store
+// it with 8 lanes per row, so every store instruction writes four whole
+// 128-byte lines -- full NVLink writes when the destination is a peer.
+// Requires seg % head_dim == 0 and head_dim % 64 == 0 (a unit never straddles
+// a head, so its destination is warp-uniform).
+__device__ __forceinline__ void scatter_unit(const Args& args, uint4* stage, uint32_t t_col, int row0, int col0,
+                                            float xs, int lane) {
+    uint32_t r[32];
+    tmem_ld32(t_col, r);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) stage[lane * 8 + (g ^ (lane & 7))] = dequant8(args, r + 8 * g, col0 + 8 * g, xs);
+    tmem_ld32(t_col + 32u, r);
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+        stage[lane * 8 + ((g + 4) ^ (lane & 7))] = dequant8(args, r + 8 * g, col0 + 32 + 8 * g, xs);
+    __syncwarp();
+    const Scatter& sc = args.sc;
+    const int t = col0 / sc.seg, within = col0 - t * sc.seg;
+    const int h = within / sc.head_dim, j = h / sc.hp;
+    const int64_t dld = (int64_t)sc.hp * sc.head_dim;
+    uint16_t* dbase = sc.dst[t * sc.world + j] + (int64_t)(h - j * sc.hp) * sc.head_dim + (within % sc.head_dim);
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const int e = p * 32 + lane, rr = e >> 3, cc = e & 7;
+        const uint4 v = stage[rr * 8 + (cc ^ (rr & 7))];
+        const int grow = row0 + rr;
+        if (grow < args.M) *reinterpret_cast<uint4*>(dbase + (sc.row_start + grow) * dld + cc * 8) = v;
+    }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -410,6 +466,8 @@ constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = B_ROWS * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int kStagingBytes = kEpiWarps * 32 * 128;  // scatter epilogue: 32 rows x 128 B per warp
+constexpr int kSmemBytesScatter = kSmemBytes + kStagingBytes;
 // instruction descriptor without its N field (bits 17-22 = N >> 3, set per launch)
 constexpr uint32_t kIdescBase = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_M >> 4) << 24);
 
@@ -455,7 +513,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-template <bool OUT_I32>
+template <bool OUT_I32, bool SCATTER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
     extern __shared__ uint8_t smem_raw[];
@@ -618,13 +676,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             float xs = 0.0f;
             if constexpr (!OUT_I32) xs = row_ok ? args.xs[row] : 0.0f;
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * MAX_TILE_N);
+            if constexpr (SCATTER) {
+                // 64-column units (TILE_N % 64 == 0 and N % 64 == 0 for this variant)
+                uint4* stage = reinterpret_cast<uint4*>(base + STAGES * STAGE_BYTES + 256) + q * (32 * 8);
 #pragma unroll 1
-            for (int c = 0; c < TILE_N / 32; ++c) {
-                const int col0 = nb * TILE_N + c * 32;
-                if (col0 >= N) break;  // warp-uniform
-                uint32_t r[32];
-                tmem_ld32(t_row + (uint32_t)(c * 32), r);
-                if (row_ok) store_chunk<OUT_I32>(args, r, row, col0, xs);
+                for (int c = 0; c < TILE_N / 64; ++c) {
+                    const int col0 = nb * TILE_N + c * 64;
+                    if (col0 >= N) break;  // warp-uniform
+                    scatter_unit(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < TILE_N / 32; ++c) {
+                    const int col0 = nb * TILE_N + c * 32;
+                    if (col0 >= N) break;  // warp-uniform
+                    uint32_t r[32];
+                    tmem_ld32(t_row + (uint32_t)(c * 32), r);
+                    if (row_ok) store_chunk<OUT_I32>(args, r, row, col0, xs);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -690,7 +759,7 @@ static int num_sms() {
 // (rounds of pair tiles over the resident pairs) x (256 + t); ties go to the
 // wider tile.  Wave quantisation picks 224 for config 0's 4096 x 5120; large M
 // keeps 256.
-static int pick_tile_n(int M, int N, int64_t pairs) {
+static int pick_tile_n(int M, int N, int64_t pairs, bool mult64 = false) {
     // H3B_GEMM_TILE_N (a multiple of 32 in 32..256) pins the width, for tuning sweeps
     static int forced = -1;
     if (forced < 0) {
@@ -698,12 +767,13 @@ static int pick_tile_n(int M, int N, int64_t pairs) {
         const int v = e ? atoi(e) : 0;
         forced = (v >= 32 && v <= 256 && v % 32 == 0) ? v : 0;
     }
-    if (forced) return forced;
+    if (forced && (!mult64 || forced % 64 == 0)) return forced;
     static const int cands[] = {256, 224, 192, 160, 128};
     const int64_t m_tiles = (M + pair::TILE_M - 1) / pair::TILE_M;
     int best = 256;
     int64_t best_cost = -1;
     for (int t : cands) {
+        if (mult64 && t % 64) continue;
         const int64_t tiles = m_tiles * ((N + t - 1) / t);
         const int64_t rounds = (tiles + pairs - 1) / pairs;
         const int64_t cost = rounds * (256 + t);
@@ -728,7 +798,7 @@ static bool force_single_cta() {
 
 // How many CTA pairs can be resident at once (a GPC may not pair every SM);
 // queried once per device and kernel variant, SM count / 2 if the query fails.
-template <bool OUT_I32>
+template <bool OUT_I32, bool SCATTER>
 static int max_pairs() {
     constexpr int kMaxDevices = 64;
     static int cache[kMaxDevices] = {};
@@ -739,8 +809,9 @@ static int max_pairs() {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = pair::kSmemBytes;
-    if (cudaOccupancyMaxActiveClusters(&n, (void*)pair::gemm_i8_pair_kernel<OUT_I32>, &cfg) != cudaSuccess || n <= 0) {
+    cfg.dynamicSmemBytes = SCATTER ? pair::kSmemBytesScatter : pair::kSmemBytes;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)pair::gemm_i8_pair_kernel<OUT_I32, SCATTER>, &cfg) != cudaSuccess ||
+        n <= 0) {
         cudaGetLastError();
         n = num_sms() / 2;
     }
@@ -756,13 +827,14 @@ static int check_device() {
     return H3B_OK;
 }
 
-template <bool OUT_I32>
+template <bool OUT_I32, bool SCATTER = false>
 static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
-    H3B_REQUIRE(xq && w && a.out, "h3b GEMM: NULL pointer");
+    H3B_REQUIRE(xq && w && (SCATTER || a.out), "h3b GEMM: NULL pointer");
     H3B_REQUIRE(a.M >= 0 && a.N > 0 && a.K > 0, "h3b GEMM: bad shape M=%d N=%d K=%d", a.M, a.N, a.K);
     H3B_REQUIRE(a.K % BK == 0, "h3b GEMM: K=%d must be a multiple of %d", a.K, BK);
     H3B_REQUIRE(a.N % 8 == 0, "h3b GEMM: N=%d must be a multiple of 8", a.N);
-    H3B_REQUIRE(aligned(xq, 16) && aligned(w, 16) && aligned(a.out, 16), "h3b GEMM: operands must be 16-byte aligned");
+    H3B_REQUIRE(aligned(xq, 16) && aligned(w, 16) && (SCATTER || aligned(a.out, 16)),
+                "h3b GEMM: operands must be 16-byte aligned");
     if (!OUT_I32) {
         H3B_REQUIRE(a.xs && a.ws && aligned(a.ws, 16), "h3b GEMM: xs/ws NULL or ws not 16-byte aligned");
         H3B_REQUIRE(!a.bias || aligned(a.bias, 16), "h3b GEMM: bias must be 16-byte aligned");
@@ -775,16 +847,18 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
     DeviceStatus ds;
     if (int rc = device_status(&ds)) return rc;
     a.status = ds.word;
-    if (a.M > BM && !force_single_cta()) {
-        // 2-CTA pairs: each CTA loads tile_n / 2 rows of B
-        H3B_CUDA_TRY(cudaFuncSetAttribute(pair::gemm_i8_pair_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          pair::kSmemBytes));
-        const int64_t pairs_max = max_pairs<OUT_I32>();
-        a.tile_n = pick_tile_n(a.M, a.N, pairs_max);
+    if (SCATTER || (a.M > BM && !force_single_cta())) {
+        // 2-CTA pairs: each CTA loads tile_n / 2 rows of B (the scatter epilogue
+        // exists in this kernel only; rows past M are masked)
+        constexpr int smem = SCATTER ? pair::kSmemBytesScatter : pair::kSmemBytes;
+        H3B_CUDA_TRY(cudaFuncSetAttribute(pair::gemm_i8_pair_kernel<OUT_I32, SCATTER>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        const int64_t pairs_max = max_pairs<OUT_I32, SCATTER>();
+        a.tile_n = pick_tile_n(a.M, a.N, pairs_max, SCATTER);
         if (int rc = make_map(&tmB, w, a.N, a.K, (uint32_t)(a.tile_n / 2))) return rc;
         const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + a.tile_n - 1) / a.tile_n);
         const int pairs = (int)(tiles < pairs_max ? tiles : pairs_max);
-        pair::gemm_i8_pair_kernel<OUT_I32><<<2 * pairs, kThreads, pair::kSmemBytes, s>>>(tmA, tmB, a);
+        pair::gemm_i8_pair_kernel<OUT_I32, SCATTER><<<2 * pairs, kThreads, smem, s>>>(tmA, tmB, a);
     } else {
         H3B_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         const int64_t tiles = (int64_t)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
@@ -817,6 +891,33 @@ extern "C" int h3b_int8_mm_i32(const int8_t* xq, const int8_t* w, int32_t* acc, 
     H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_i32: shape out of range");
     gemm::Args a{nullptr, nullptr, nullptr, acc, (int)M, (int)N, (int)K, nullptr};
     return gemm::launch<true>(xq, w, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_int8_mm_scaled_a2a(const int8_t* xq, const int8_t* w, const float* xs, const float* ws,
+                                      const void* bias, int64_t M, int64_t N, int64_t K, void* const* dst,
+                                      int64_t row_start, int64_t seg_cols, int64_t head_dim, int64_t heads_per_rank,
+                                      int world, void* stream) {
+    H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_scaled_a2a: shape out of range");
+    H3B_REQUIRE(dst && world >= 1 && world <= gemm::kMaxScatterWorld && row_start >= 0,
+                "h3b_int8_mm_scaled_a2a: bad dst / world=%d / row_start", world);
+    H3B_REQUIRE(head_dim > 0 && head_dim % 64 == 0 && seg_cols > 0 && seg_cols % head_dim == 0 && N % seg_cols == 0 &&
+                    N / seg_cols <= gemm::kMaxScatterSegs && seg_cols / head_dim == heads_per_rank * world,
+                "h3b_int8_mm_scaled_a2a: N=%lld seg=%lld head_dim=%lld heads_per_rank=%lld world=%d do not describe "
+                "whole heads split evenly over the ranks (head_dim %% 64 == 0, at most %d segments)",
+                (long long)N, (long long)seg_cols, (long long)head_dim, (long long)heads_per_rank, world,
+                gemm::kMaxScatterSegs);
+    gemm::Args a{xs, ws, static_cast<const uint16_t*>(bias), nullptr, (int)M, (int)N, (int)K, nullptr};
+    const int segs = (int)(N / seg_cols);
+    for (int i = 0; i < segs * world; ++i) {
+        H3B_REQUIRE(dst[i] && aligned(dst[i], 16), "h3b_int8_mm_scaled_a2a: dst[%d] NULL or not 16-byte aligned", i);
+        a.sc.dst[i] = static_cast<uint16_t*>(dst[i]);
+    }
+    a.sc.row_start = row_start;
+    a.sc.seg = (int)seg_cols;
+    a.sc.head_dim = (int)head_dim;
+    a.sc.hp = (int)heads_per_rank;
+    a.sc.world = world;
+    return gemm::launch<false, true>(xq, w, a, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int h3b_int8_linear(const void* x, int64_t M, int64_t K, const int8_t* w, const float* ws,

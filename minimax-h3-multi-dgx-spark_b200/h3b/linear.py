@@ -10,7 +10,7 @@ kernels run on the current CUDA stream, shape/dtype violations raise.
 """
 import torch
 
-from ._lib import check, lib, ptr, require_cuda, stream_of
+from ._lib import check, lib, ptr, ptr_array, require_cuda, stream_of
 from .trace import span
 
 
@@ -81,6 +81,31 @@ def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
         check(lib.h3b_int8_mm_scaled(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
               "h3b_int8_mm_scaled")
     return out
+
+
+def int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst_ptrs, row_start, seg, head_dim, heads_per_rank, world):
+    """int8_mm_scaled whose epilogue stores column n of the [M,N] product into
+    the receive buffer of the rank owning its head (h3b_int8_mm_scaled_a2a):
+    dst_ptrs = device addresses [segment * world + rank] of bf16 buffers with
+    rows of heads_per_rank*head_dim elements and at least row_start + M rows
+    (the caller guarantees their size).  Returns nothing; the receivers see the
+    rows after a peer barrier."""
+    M, N, K = _gemm_checks(xq, w)
+    xs = xs.reshape(-1)
+    if xs.dtype != torch.float32 or ws.dtype != torch.float32 or xs.numel() != M or ws.numel() != N:
+        raise ValueError("int8_mm_scaled_a2a: xs must be fp32 [M] / [M,1] and ws fp32 [N]")
+    xs, ws = xs.contiguous(), ws.contiguous()
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != N:
+            raise ValueError("int8_mm_scaled_a2a: bias must be bf16 [N]")
+        bias = bias.contiguous()
+    if len(dst_ptrs) != (N // seg) * world:
+        raise ValueError("int8_mm_scaled_a2a: one destination per segment and rank")
+    arr, keep = ptr_array(dst_ptrs)
+    with span("gemm_a2a", 2 * M * N * K):
+        check(lib.h3b_int8_mm_scaled_a2a(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), M, N, K, arr, row_start, seg,
+                                         head_dim, heads_per_rank, world, stream_of(xq)), "h3b_int8_mm_scaled_a2a")
+    del keep
 
 
 def int8_mm_i32(xq, w, out=None):

@@ -30,6 +30,7 @@ Weights are int8 with per-output-channel fp32 scales and bf16 biases, drawn
 from a seeded generator on the target device.  Attention stays PyTorch's
 scaled_dot_product_attention, as in the reference.
 """
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -132,15 +133,22 @@ def self_attention(cfg, p, hq, ctx, overlap_groups=None):
     environment (sp.overlap_groups), 0 or 1 disables it."""
     s = hq[0].shape[0]
     D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
+    sharded = ctx is not None and ctx.world > 1
+    hp = H // ctx.world if sharded else H
+    n = (sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups) if sharded else 0
+    overlap = n > 1 and hp % n == 0
+    if sharded and not overlap and ctx.exchange == "p2p" and FUSED_QKV_EXCHANGE:
+        # the qkv GEMM's epilogue stores q, k, v straight into the owners' buffers
+        q, k, v = ctx.peer.gemm_fwd(hq[0], hq[1], p.qkv.w, p.qkv.ws, p.qkv.b, ctx)
+        o = sdpa_heads(q, k, v)
+        return _lin(sp.a2a_scatter_seq_gather_heads(o, ctx), p.out)
     qkv = _lin_q(hq, p.qkv)  # [s, 3D]
     q = qkv[:, :D].view(s, H, Dh)
     k = qkv[:, D:2 * D].view(s, H, Dh)
     v = qkv[:, 2 * D:].view(s, H, Dh)
-    if ctx is None or ctx.world == 1:
+    if not sharded:
         return _lin(sdpa_heads(q, k, v), p.out)
-    hp = H // ctx.world
-    n = sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups
-    if n > 1 and hp % n == 0:
+    if overlap:
         return _lin(sp.sp_attention_overlap(q, k, v, ctx, sdpa_heads, n), p.out)
     q, k, v = sp.a2a_gather_qkv(q, k, v, ctx)  # [S, H/P, Dh] each
     o = sdpa_heads(q, k, v)  # [S, (H/P)*Dh]
@@ -158,6 +166,12 @@ def cross_attention(cfg, p, hq, text):
     v = kv[:, D:].view(t, H, Dh)
     return _lin(sdpa_heads(q, k, v), p.cout)
 
+
+# With the peer-memory exchange the qkv projection's epilogue writes q, k and v
+# straight into the receive buffers of the ranks owning their heads
+# (PeerExchange.gemm_fwd), so the forward exchange needs no copy kernel.
+# H3B_FUSED_QKV_EXCHANGE=0 selects GEMM then exchange kernel.
+FUSED_QKV_EXCHANGE = os.environ.get("H3B_FUSED_QKV_EXCHANGE", "1") != "0"
 
 # The modulated activations feed only INT8 linears, so the norm kernels can emit
 # their int8 codes and scales directly (norm_mod_quant / gate_norm_mod_quant_)

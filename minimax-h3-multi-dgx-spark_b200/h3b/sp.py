@@ -347,6 +347,26 @@ class PeerExchange:
                                       g * w * es, self.world, stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
         del k1, k2
 
+    def gemm_fwd(self, xq, xs, w, ws, bias, ctx):
+        """A projection fused with the forward exchange (h3b_int8_mm_scaled_a2a):
+        the [s_local, n*H*Dh] product of the quantised rows (xq, xs) and w
+        (n = 1..3 segments, e.g. the fused q|k|v projection) is stored by the
+        GEMM's epilogue straight into every rank's receive buffers.  Returns the
+        n views [S, H/P, Dh] of this rank's receive buffers."""
+        from .linear import int8_mm_scaled_a2a
+        D = self.heads * self.head_dim
+        nseg = w.shape[0] // D
+        if w.shape[0] != nseg * D or not 1 <= nseg <= len(self.recv) or ctx.seq_len > self.seq_len:
+            raise ValueError("gemm_fwd: the projection does not match the PeerExchange buffers")
+        if xq.shape[0] != ctx.local:
+            raise ValueError("gemm_fwd: xq must hold this rank's rows")
+        dst = [self.peer_recv[t][j] for t in range(nseg) for j in range(self.world)]
+        self.barrier(xq)
+        int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst, ctx.start, D, self.head_dim, self.heads // self.world,
+                           self.world)
+        self.barrier(xq)
+        return self.recv_views(nseg, ctx)
+
     def fwd(self, tensors, ctx):
         """tensors: n x [s_local, H, D] -> n views [S, H/P, D] of the receive buffers."""
         self.barrier(tensors[0])

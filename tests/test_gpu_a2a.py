@@ -1,9 +1,10 @@
 """GPU parity of the Ulysses all-to-all kernels on one GPU (bit-exact).
 
 Pack/unpack are checked against the numpy restatement of sp_forward.py:185/198.
-The peer-memory exchange kernels are checked by running every rank's launch on
-one GPU with all "peer" buffers local: the copy kernels never wait on anything,
-so this exercises their full index arithmetic without a second GPU.  The
+The peer-memory exchange kernels (and the qkv GEMM whose epilogue does the
+exchange) are checked by running every rank's launch on one GPU with all
+"peer" buffers local: they never wait on anything, so this exercises their
+full index arithmetic without a second GPU.  The
 barrier kernel's bounded wait is checked by letting it wait for a flag that
 nothing sets.  Multi-GPU runs are in test_gpu_multi.py.
 """
@@ -150,6 +151,38 @@ def test_pack_unpack_head_groups(world, s_local, groups):
         np.testing.assert_array_equal(bits(send), kb[:, :, g].transpose(1, 0, 2))
         h3b.unpack(send, out=final[:, g * w:], block=hp * DH)
     np.testing.assert_array_equal(bits(final), bits(qkv)[:, H * DH:2 * H * DH])
+
+
+@pytest.mark.parametrize("world,S,heads,K", [(2, 1001, 40, 256), (4, 4130, 40, 384), (8, 2000, 40, 256),
+                                             (1, 300, 8, 128), (2, 20000, 40, 5120), (8, 130, 16, 128)])
+def test_gemm_a2a_emulated(world, S, heads, K):
+    """The qkv GEMM with the exchange in its epilogue (h3b_int8_mm_scaled_a2a),
+    every rank's launch on one GPU: each rank's receive buffers must equal the
+    forward exchange (sp_layout.a2a_fwd) of the unfused GEMM outputs, and every
+    receive row must be written (the buffers start as a sentinel pattern)."""
+    from gpu_util import gen
+    splits = sp_layout.splits(S, world)
+    starts = sp_layout.starts(S, world)
+    hp = heads // world
+    D = heads * DH
+    g = gen(world * 1000 + S + K)
+    w = torch.randint(-127, 128, (3 * D, K), generator=g, dtype=torch.int8).to(DEV)
+    ws = (torch.rand(3 * D, generator=g) * 9e-3 + 1e-3).to(DEV)
+    bias = (torch.randn(3 * D, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    xq = [torch.randint(-127, 128, (n, K), generator=g, dtype=torch.int8).to(DEV) for n in splits]
+    xs = [(torch.rand(n, 1, generator=g) * 0.05 + 1e-3).to(DEV) for n in splits]
+    recv = [[torch.full((S, hp * DH), -7.0, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+            for _ in range(3)]
+    dst = [recv[t][j].data_ptr() for t in range(3) for j in range(world)]
+    for r in range(world):
+        h3b.int8_mm_scaled_a2a(xq[r], w, xs[r], ws, bias, dst, starts[r], D, DH, hp, world)
+    ys = [h3b.int8_mm_scaled(xq[r], w, xs[r], ws, bias=bias) for r in range(world)]
+    torch.cuda.synchronize()
+    assert h3b.status() == 0
+    for t in range(3):
+        ref = sp_layout.a2a_fwd([bits(y)[:, t * D:(t + 1) * D].reshape(-1, heads, DH) for y in ys], world)
+        for j in range(world):
+            np.testing.assert_array_equal(bits(recv[t][j]).reshape(S, hp, DH), ref[j], err_msg=f"t={t} j={j}")
 
 
 def test_peer_barrier_times_out_and_reports():
