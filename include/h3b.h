@@ -195,6 +195,18 @@ H3B_API int h3b_a2a_pack(const void *t, int64_t t_ld, void *send, int64_t s_loca
 H3B_API int h3b_a2a_unpack(const void *recv, void *out, int64_t out_ld, int64_t s_local, int64_t chunk_bytes,
                            int64_t block_bytes, int world, void *stream);
 
+/* Inverse exchange fused with the activation quantiser of the attention
+ * output projection: local row m (of M) is the concatenation over ranks
+ * j = 0 .. P-1 of row row_start + m of src[j] (rank j's attention output
+ * [S, chunk], bf16, rows src_ld bytes apart; a peer's memory for j != this
+ * rank), i.e. the row the inverse exchange would deliver; it is quantised
+ * exactly as h3b_quant_rowwise (K = P * chunk_bytes / 2 <= 32768) into
+ * xq [M, K] / xs [M].  Bracket with h3b_peer_barrier (every src complete).
+ * Replaces a2a_scatter_seq_gather_heads, sp_forward.py:191-198, followed by the
+ * out projection's quantisation, h3_linear_fast_patch.py:89-95. */
+H3B_API int h3b_a2a_inv_quant(const void *const *src, int64_t src_ld, int64_t row_start, int64_t M,
+                              int64_t chunk_bytes, int world, int8_t *xq, float *xs, void *stream);
+
 /* CUDA IPC plumbing for the peer-memory all-to-all.  h3b_ipc_handle returns
  * the 64-byte cudaIpcMemHandle of the allocation holding dev_ptr and
  * dev_ptr's offset inside it; h3b_ipc_open maps a peer's allocation and

@@ -12,6 +12,12 @@
 // polynomial as one fused multiply-add, tanhf, 0.5*x*(1+t)), so the codes equal
 // quant(F.gelu(u, approximate="tanh")) bit for bit without the bf16 GELU output
 // ever reaching HBM.
+//
+// Gather variant (the inverse Ulysses exchange fused with the quantiser of the
+// attention output projection): row m is assembled from every rank's attention
+// output rows, read over NVLink from the peers' buffers, so the exchanged rows
+// never land in a staging buffer; codes and scales are those of the gathered
+// row, bit for bit.
 #include "quant_common.cuh"
 
 namespace h3b {
@@ -30,9 +36,21 @@ __device__ __forceinline__ uint32_t gelu2(uint32_t v) {
     return pack_bf16x2(gelu_tanh(bf16_lo(v)), gelu_tanh(bf16_hi(v)));
 }
 
-template <int VPT, int NT, Act ACT>
+constexpr int kMaxGatherRanks = 8;
+
+// Row source of the inverse-exchange quantiser: vector j of local row m is
+// vector j % cv of row (row0 + m) of rank j / cv's buffer src[j / cv] (rows
+// ldv vectors apart; a peer's memory for the other ranks).
+struct GatherRows {
+    const uint4* src[kMaxGatherRanks];
+    int64_t row0, ldv;
+    int cv;
+};
+
+template <int VPT, int NT, Act ACT, bool GATHER>
 __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
-                                                           int8_t* __restrict__ xq, float* __restrict__ xs) {
+                                                           int8_t* __restrict__ xq, float* __restrict__ xs,
+                                                           GatherRows g) {
     const int64_t row = blockIdx.x;
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
     const int nvec = K >> 3;
@@ -41,7 +59,14 @@ __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __res
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         const int j = threadIdx.x + i * NT;
-        if (j < nvec) v[i] = xr[j];
+        if (j < nvec) {
+            if constexpr (GATHER) {
+                const int rk = j / g.cv;
+                v[i] = g.src[rk][(g.row0 + row) * g.ldv + (j - rk * g.cv)];
+            } else {
+                v[i] = xr[j];
+            }
+        }
     }
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -80,13 +105,13 @@ __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __res
     }
 }
 
-template <int NT, Act ACT>
+template <int NT, Act ACT, bool GATHER = false>
 static void launch_quant(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
-                         cudaStream_t s) {
+                         cudaStream_t s, GatherRows g = GatherRows{}) {
     dim3 grid((unsigned)M), block(NT);
     switch (vpt) {
 #define H3B_QCASE(V) \
-    case V: quant_rowwise_kernel<V, NT, ACT><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
+    case V: quant_rowwise_kernel<V, NT, ACT, GATHER><<<grid, block, 0, s>>>(x, ldx, K, xq, xs, g); break;
         H3B_QCASE(1) H3B_QCASE(2) H3B_QCASE(3) H3B_QCASE(4) H3B_QCASE(5) H3B_QCASE(6) H3B_QCASE(7) H3B_QCASE(8)
         H3B_QCASE(10) H3B_QCASE(12) H3B_QCASE(14) H3B_QCASE(16)
 #undef H3B_QCASE
@@ -128,6 +153,38 @@ int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, 
     return quant_impl<Act::kNone>(x, ldx, M, K, xq, xs, s, "h3b_quant_rowwise");
 }
 
+static int gather_quant(const void* const* src, int64_t src_ld, int64_t row_start, int64_t M, int64_t chunk_bytes,
+                        int world, int8_t* xq, float* xs, cudaStream_t s) {
+    const char* who = "h3b_a2a_inv_quant";
+    H3B_REQUIRE(src && xq && xs && world >= 1 && world <= kMaxGatherRanks, "%s: bad arguments (world=%d)", who, world);
+    H3B_REQUIRE(chunk_bytes > 0 && chunk_bytes % 16 == 0 && src_ld >= chunk_bytes && src_ld % 16 == 0,
+                "%s: chunk %lld / src_ld %lld bytes must be multiples of 16", who, (long long)chunk_bytes,
+                (long long)src_ld);
+    const int64_t K = world * chunk_bytes / 2;
+    H3B_REQUIRE(K <= 32768 && M >= 0 && M < (1ll << 31) && row_start >= 0, "%s: K=%lld / M=%lld out of range", who,
+                (long long)K, (long long)M);
+    H3B_REQUIRE(aligned(xq, 8), "%s: xq must be 8-byte aligned", who);
+    GatherRows g{};
+    for (int j = 0; j < world; ++j) {
+        H3B_REQUIRE(src[j] && aligned(src[j], 16), "%s: src[%d] NULL or not 16-byte aligned", who, j);
+        g.src[j] = static_cast<const uint4*>(src[j]);
+    }
+    g.row0 = row_start;
+    g.ldv = src_ld / 16;
+    g.cv = (int)(chunk_bytes / 16);
+    if (M == 0) return H3B_OK;
+    const int nvec = (int)(K / 8);
+    int vpt = pick_vpt((nvec + 127) / 128);
+    if (vpt > 0) {
+        launch_quant<128, Act::kNone, true>(vpt, nullptr, 0, M, (int)K, xq, xs, s, g);
+    } else {
+        vpt = pick_vpt((nvec + 255) / 256);
+        launch_quant<256, Act::kNone, true>(vpt, nullptr, 0, M, (int)K, xq, xs, s, g);
+    }
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
+}
+
 }  // namespace h3b
 
 extern "C" int h3b_quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs,
@@ -139,4 +196,9 @@ extern "C" int h3b_gelu_quant(const void* u, int64_t ldu, int64_t M, int64_t K, 
                               void* stream) {
     return h3b::quant_impl<h3b::Act::kGeluTanh>(u, ldu, M, K, xq, xs, static_cast<cudaStream_t>(stream),
                                                 "h3b_gelu_quant");
+}
+
+extern "C" int h3b_a2a_inv_quant(const void* const* src, int64_t src_ld, int64_t row_start, int64_t M,
+                                 int64_t chunk_bytes, int world, int8_t* xq, float* xs, void* stream) {
+    return h3b::gather_quant(src, src_ld, row_start, M, chunk_bytes, world, xq, xs, static_cast<cudaStream_t>(stream));
 }

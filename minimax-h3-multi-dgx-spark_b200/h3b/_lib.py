@@ -43,6 +43,7 @@ SIGNATURES = [
     ("h3b_ipc_close", _I32, [_P]),
     ("h3b_peer_barrier", _I32, [_PP, _I32, _I32, _U32, _I64, _P]),
     ("h3b_a2a_fwd_p2p", _I32, [_I32, _PP, _I64, _PP, _I64, _I64, _I64, _I64, _I64, _I32, _P]),
+    ("h3b_a2a_inv_quant", _I32, [_PP, _I64, _I64, _I64, _I64, _I32, _P, _P, _P]),
     ("h3b_a2a_inv_p2p", _I32, [_P, _I64, _PP, ctypes.POINTER(ctypes.c_int64), _I64, _I64, _I64, _I32, _P]),
 ]
 

@@ -117,12 +117,18 @@ def _lin_q(q, l):
     return _mm8(xq, l.w, xs, l.ws, bias=l.b)
 
 
-def sdpa_heads(q, k, v):
-    """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h*Dh] via SDPA on [1, h, S, Dh] views."""
+def sdpa(q, k, v):
+    """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h, Dh] (a strided view of
+    SDPA's [1, h, Sq, Dh] output) via SDPA on [1, h, S, Dh] views."""
     o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
                                        v.transpose(0, 1).unsqueeze(0))
+    return o.squeeze(0).transpose(0, 1)
+
+
+def sdpa_heads(q, k, v):
+    """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h*Dh] via SDPA on [1, h, S, Dh] views."""
     sq, h, dh = q.shape
-    return o.squeeze(0).transpose(0, 1).reshape(sq, h * dh)
+    return sdpa(q, k, v).reshape(sq, h * dh)
 
 
 def self_attention(cfg, p, hq, ctx, overlap_groups=None):
@@ -137,11 +143,11 @@ def self_attention(cfg, p, hq, ctx, overlap_groups=None):
     hp = H // ctx.world if sharded else H
     n = (sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups) if sharded else 0
     overlap = n > 1 and hp % n == 0
-    if sharded and not overlap and ctx.exchange == "p2p" and FUSED_QKV_EXCHANGE:
-        # the qkv GEMM's epilogue stores q, k, v straight into the owners' buffers
+    if sharded and not overlap and ctx.exchange == "p2p" and FUSED_EXCHANGE:
+        # the qkv GEMM's epilogue stores q, k, v straight into the owners' buffers;
+        # the out projection's quantiser gathers its rows from every rank's output
         q, k, v = ctx.peer.gemm_fwd(hq[0], hq[1], p.qkv.w, p.qkv.ws, p.qkv.b, ctx)
-        o = sdpa_heads(q, k, v)
-        return _lin(sp.a2a_scatter_seq_gather_heads(o, ctx), p.out)
+        return _lin_q(ctx.peer.inv_quant(sdpa(q, k, v), ctx), p.out)
     qkv = _lin_q(hq, p.qkv)  # [s, 3D]
     q = qkv[:, :D].view(s, H, Dh)
     k = qkv[:, D:2 * D].view(s, H, Dh)
@@ -169,9 +175,11 @@ def cross_attention(cfg, p, hq, text):
 
 # With the peer-memory exchange the qkv projection's epilogue writes q, k and v
 # straight into the receive buffers of the ranks owning their heads
-# (PeerExchange.gemm_fwd), so the forward exchange needs no copy kernel.
-# H3B_FUSED_QKV_EXCHANGE=0 selects GEMM then exchange kernel.
-FUSED_QKV_EXCHANGE = os.environ.get("H3B_FUSED_QKV_EXCHANGE", "1") != "0"
+# (PeerExchange.gemm_fwd) and the out projection's quantiser reads its rows
+# from every rank's attention output (PeerExchange.inv_quant), so neither
+# exchange needs a copy kernel.  H3B_FUSED_EXCHANGE=0 selects the separate
+# exchange kernels.
+FUSED_EXCHANGE = os.environ.get("H3B_FUSED_EXCHANGE", "1") != "0"
 
 # The modulated activations feed only INT8 linears, so the norm kernels can emit
 # their int8 codes and scales directly (norm_mod_quant / gate_norm_mod_quant_)

@@ -237,8 +237,10 @@ class PeerExchange:
 
     Collective to construct (every rank of `group` calls it with the same
     arguments) and to `close()`.  Buffers: n_fwd receive buffers of
-    [seq_len, chunk] and one inverse output buffer of [max_local, world*chunk]
-    (chunk = heads/world * head_dim elements), plus a uint32 [world] flag array.
+    [seq_len, chunk], one inverse output buffer of [max_local, world*chunk],
+    one attention output buffer of [seq_len, chunk] that the peers read
+    (inv_quant) (chunk = heads/world * head_dim elements), plus a uint32
+    [world] flag array.
     """
 
     def __init__(self, group, rank, world, seq_len, heads, head_dim, dtype=torch.bfloat16, n_fwd=3,
@@ -256,28 +258,21 @@ class PeerExchange:
         self.timeout_ns = int(timeout_s * 1e9)
         self.recv = [torch.empty((seq_len, self.chunk), dtype=dtype, device=dev) for _ in range(n_fwd)]
         self.out = torch.empty((max_local, world * self.chunk), dtype=dtype, device=dev)
+        self.obuf = torch.empty((seq_len, self.chunk), dtype=dtype, device=dev)  # attention output, pulled by peers
         self.flags = torch.zeros(world, dtype=torch.int32, device=dev)
         self.epoch = 0
         self.comm = None  # side stream of the exchange/attention overlap
         self._bases = []
-        mine = [self._handle(t) for t in self.recv + [self.out, self.flags]]
+        shared = self.recv + [self.out, self.obuf, self.flags]
+        mine = [self._handle(t) for t in shared]
         gathered = [None] * world
         dist.all_gather_object(gathered, mine, group=group)
-        self.peer_recv = [[None] * world for _ in range(n_fwd)]
-        self.peer_out = [None] * world
-        self.peer_flags = [None] * world
+        peer = [[None] * world for _ in shared]  # peer[buffer][rank] = address in this process
         for j in range(world):
             for idx, (hb, off) in enumerate(gathered[j]):
-                if j == rank:
-                    p = (self.recv + [self.out, self.flags])[idx].data_ptr()
-                else:
-                    p = self._open(hb, off)
-                if idx < n_fwd:
-                    self.peer_recv[idx][j] = p
-                elif idx == n_fwd:
-                    self.peer_out[j] = p
-                else:
-                    self.peer_flags[j] = p
+                peer[idx][j] = shared[idx].data_ptr() if j == rank else self._open(hb, off)
+        self.peer_recv = peer[:n_fwd]
+        self.peer_out, self.peer_obuf, self.peer_flags = peer[n_fwd], peer[n_fwd + 1], peer[n_fwd + 2]
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
@@ -397,6 +392,34 @@ class PeerExchange:
         self.inv_copy(t, ctx)
         self.barrier(t)
         return self.out[: ctx.local]
+
+    def inv_quant(self, o, ctx):
+        """Inverse exchange fused with the out projection's quantiser.
+
+        o: this rank's attention output [S, H/P, Dh] or [S, (H/P)*Dh] (any
+        strides).  It is copied into this rank's shared output buffer; after a
+        barrier every rank quantises its own rows, each gathered from all ranks'
+        buffers over NVLink (h3b_a2a_inv_quant).  Returns (codes [s_local, H*Dh]
+        int8, scales [s_local, 1] fp32), equal to quant_rowwise of the row the
+        inverse exchange delivers.  The shared buffer is reused by the next call:
+        every rank's gather of it precedes that rank's arrival at the next
+        exchange's first barrier, which precedes the next copy into it."""
+        require_cuda(o)
+        S, hp = ctx.seq_len, self.heads // self.world
+        if S > self.seq_len:
+            raise ValueError("inv_quant: sequence longer than the PeerExchange buffers")
+        self.obuf[:S].view(S, hp, self.head_dim).copy_(o.reshape(S, hp, self.head_dim))
+        self.barrier(o)
+        K = self.heads * self.head_dim
+        xq = torch.empty((ctx.local, K), dtype=torch.int8, device=o.device)
+        xs = torch.empty((ctx.local, 1), dtype=torch.float32, device=o.device)
+        es = self.obuf.element_size()
+        arr, keep = ptr_array(self.peer_obuf)
+        with span("quant_a2a", ctx.local * K * (es + 1) + 4 * ctx.local):
+            check(lib.h3b_a2a_inv_quant(arr, self.chunk * es, ctx.start, ctx.local, self.chunk * es, self.world,
+                                        ptr(xq), ptr(xs), stream_of(o)), "h3b_a2a_inv_quant")
+        del keep
+        return xq, xs
 
     def attention_overlap(self, q, k, v, ctx, attn, groups):
         """sp_attention_overlap over peer memory.  The exchanges run on a

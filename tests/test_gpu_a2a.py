@@ -2,7 +2,7 @@
 
 Pack/unpack are checked against the numpy restatement of sp_forward.py:185/198.
 The peer-memory exchange kernels (and the qkv GEMM whose epilogue does the
-exchange) are checked by running every rank's launch on one GPU with all
+forward exchange, and the quantiser that gathers the inverse one) are checked by running every rank's launch on one GPU with all
 "peer" buffers local: they never wait on anything, so this exercises their
 full index arithmetic without a second GPU.  The
 barrier kernel's bounded wait is checked by letting it wait for a flag that
@@ -183,6 +183,31 @@ def test_gemm_a2a_emulated(world, S, heads, K):
         ref = sp_layout.a2a_fwd([bits(y)[:, t * D:(t + 1) * D].reshape(-1, heads, DH) for y in ys], world)
         for j in range(world):
             np.testing.assert_array_equal(bits(recv[t][j]).reshape(S, hp, DH), ref[j], err_msg=f"t={t} j={j}")
+
+
+@pytest.mark.parametrize("world,S", [(2, 1001), (4, 4130), (8, 2000), (8, 9)])
+def test_inv_quant_emulated(world, S):
+    """The out projection's quantiser gathering its rows from every rank's
+    attention output (h3b_a2a_inv_quant), every rank's launch on one GPU: codes
+    and scales equal quant_rowwise of the rows the inverse exchange delivers."""
+    splits = sp_layout.splits(S, world)
+    starts = sp_layout.starts(S, world)
+    chunk = H // world * DH
+    outs = [randn_bf16((S, chunk), seed=6000 + j, scale=1.0 + j) for j in range(world)]
+    od = [o.to(DEV) for o in outs]
+    ref_rows = sp_layout.a2a_inv([bits(o) for o in outs], world)
+    src, keep = ptr_array([o.data_ptr() for o in od])
+    for r in range(world):
+        xq = torch.empty(splits[r], H * DH, dtype=torch.int8, device=DEV)
+        xs = torch.empty(splits[r], 1, dtype=torch.float32, device=DEV)
+        check(lib.h3b_a2a_inv_quant(src, chunk * 2, starts[r], splits[r], chunk * 2, world,
+                                    ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(xs.data_ptr()), _stream()),
+              "inv_quant")
+        rows = torch.from_numpy(ref_rows[r].view(np.int16)).view(torch.bfloat16).to(DEV)
+        q_ref, s_ref = h3b.quant_rowwise(rows)
+        torch.cuda.synchronize()
+        assert torch.equal(xq, q_ref), f"rank {r}: codes differ"
+        assert torch.equal(xs.reshape(-1), s_ref.reshape(-1)), f"rank {r}: scales differ"
 
 
 def test_peer_barrier_times_out_and_reports():

@@ -11,9 +11,9 @@ restatement locally.  Checked bit-exactly:
   * the same exchanges done the reference's way (reshape + all_to_all_single);
   * the exchange/attention overlap by head groups (both back ends, several
     group counts) against the plain exchange;
-  * one full DiT block (p2p exchange: qkv GEMM with the exchange in its
-    epilogue, GEMM then exchange kernel, and the overlap) against the eager
-    PyTorch block using all_to_all_single.
+  * one full DiT block (p2p exchange: fused into the qkv GEMM's epilogue and
+    the out projection's quantiser, as separate kernels, and the overlap)
+    against the eager PyTorch block using all_to_all_single.
 """
 import os
 import socket
@@ -115,12 +115,12 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize(dev)
         bad = (y.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
         assert bad == 0, f"block at world {world}: {bad} elements differ"
-        # the same block with the qkv projection and the forward exchange unfused
-        hm.FUSED_QKV_EXCHANGE = False
+        # the same block with the exchanges as separate kernels
+        hm.FUSED_EXCHANGE = False
         try:
             y3 = hm.block_forward(cfg, p, x.clone(), ridx, ctx)
         finally:
-            hm.FUSED_QKV_EXCHANGE = True
+            hm.FUSED_EXCHANGE = True
         torch.cuda.synchronize(dev)
         bad = (y3.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
         assert bad == 0, f"unfused-exchange block at world {world}: {bad} elements differ"
