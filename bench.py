@@ -2,7 +2,7 @@
 """Benchmark of the H3 DiT hot path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dit_block|dit_step|linear|fused|a2a] [--seq S] [--exchange p2p|nccl]
+                    [--workload dit_block|dit_step|linear|fused|a2a|qkv_a2a] [--seq S] [--exchange p2p|nccl]
                     [--overlap G]
 
 Default workload (dit_block): one synthetic DiT block of the benchmark's
@@ -27,7 +27,9 @@ cores on a bounded sample of the same workload (rank 0, N=1 only).
 `--impl reference` prints the CPU reference path's line instead (rank 0 only).
 The other workloads (linear = single INT8 linear of config 0, fused = the
 fused chain of config 1, a2a = the Ulysses exchange of config 2, dit_step =
-the 40-block step of config 4) are available for measurements by hand.
+the 40-block step of config 4, qkv_a2a = one rank's qkv GEMM with the forward
+exchange in its epilogue, the ranks' buffers emulated on one GPU) are
+available for measurements by hand.
 """
 import argparse
 import json
@@ -60,7 +62,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a"], default="dit_block")
+    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a"],
+                    default="dit_block")
+    ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
     ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
     ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / S of the fused workload")
@@ -459,6 +463,44 @@ def linear_workload(args, dev):
     return ms, clocks, tr.summary(args.steps), tr.launches / args.steps
 
 
+def qkv_a2a_workload(args, dev):
+    """One rank's qkv projection with the forward exchange in the GEMM's epilogue
+    (h3b_int8_mm_scaled_a2a), on one GPU: the P ranks' receive buffers are all
+    local here, so this times the kernel with the scatter epilogue against the
+    plain GEMM of the same shape (the NVLink leg is measured by the dit_block
+    workload at N > 1)."""
+    import h3b
+    from h3b.trace import Trace
+    P = args.peers
+    M, D, H, Dh = args.rows or 16000, 5120, 40, 128
+    hp = H // P
+    g = torch.Generator().manual_seed(0)
+    xq = torch.randint(-127, 128, (M, D), generator=g, dtype=torch.int8).to(dev)
+    xs = (torch.rand(M, 1, generator=g) * 0.05 + 1e-3).to(dev)
+    w = torch.randint(-127, 128, (3 * D, D), generator=g, dtype=torch.int8).to(dev)
+    ws = (torch.rand(3 * D, generator=g) * 9e-3 + 1e-3).to(dev)
+    b = (torch.randn(3 * D, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    recv = [torch.empty(M, hp * Dh, dtype=torch.bfloat16, device=dev) for _ in range(3 * P)]  # rank 0's rows
+    dst = [t.data_ptr() for t in recv]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        flush.zero_()
+        h3b.int8_mm_scaled_a2a(xq, w, xs, ws, b, dst, 0, D, Dh, hp, P)
+
+    def step_plain():
+        flush.zero_()
+        h3b.int8_mm_scaled(xq, w, xs, ws, bias=b)
+
+    ms, clocks = timed(step, args.steps, args.warmup, 1, dev)
+    for _ in range(args.warmup):
+        step_plain()
+    with Trace() as tr:
+        timed(step, args.steps, 0, 1, dev, sample_clocks=False)
+        timed(step_plain, args.steps, 0, 1, dev, sample_clocks=False)
+    return M, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
+
+
 def fused_workload(args, dev):
     import h3b
     from h3b.trace import Trace
@@ -572,6 +614,24 @@ def main():
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
                     "config": {"workload": "linear", "M": M, "N": 5120, "K": 5120, "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
+                    "breakdown": breakdown(spans, pk)}
+        elif args.workload == "qkv_a2a":
+            M, ms, clocks, spans, launches = qkv_a2a_workload(args, dev)
+            ops = 2 * M * 3 * 5120 * 5120
+            ga = spans["gemm_a2a"]
+            peak = 2.0 * pk["bf16_tflops"]
+            ach = ga["work"] / (ga["ms"] * 1e-3) / 1e12
+            line = {"metric": "qkv INT8 GEMM with the exchange in its epilogue, TOPS",
+                    "value": round(ops / (ms * 1e-3) / 1e12, 1),
+                    "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
+                    "config": {"workload": "qkv_a2a", "M": M, "N": 3 * 5120, "K": 5120, "peers_emulated": args.peers,
+                               "l2": "256 MB flush per step"},
+                    "roofline": {"kernel": "gemm_i8_pair_kernel<false, SCATTER> (tcgen05 cta_group::2 kind::i8 + "
+                                           "scatter epilogue)", "bound": "tensor", "achieved": round(ach, 1),
+                                 "peak": round(peak, 1), "unit": "TOPS", "frac": round(ach / peak, 4),
+                                 "traffic": None},
+                    "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
         elif args.workload == "fused":
             ms, clocks, spans, launches = fused_workload(args, dev)

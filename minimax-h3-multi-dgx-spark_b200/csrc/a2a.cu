@@ -99,7 +99,7 @@ struct BarrierArgs {
 
 // Thread j signals rank j (slot [rank] of its array) and then waits for rank
 // j's signal in slot [j] of this rank's array.  Bounded by timeout_ns.
-__global__ void peer_barrier_kernel(BarrierArgs a, int world, int rank, uint32_t epoch, int64_t timeout_ns,
+__global__ void peer_barrier_kernel(const __grid_constant__ BarrierArgs a, int world, int rank, uint32_t epoch, int64_t timeout_ns,
                                     int* status) {
     const int j = threadIdx.x;
     if (j >= world) return;

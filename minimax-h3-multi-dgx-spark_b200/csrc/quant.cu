@@ -50,7 +50,7 @@ struct GatherRows {
 template <int VPT, int NT, Act ACT, bool GATHER>
 __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                                            int8_t* __restrict__ xq, float* __restrict__ xs,
-                                                           GatherRows g) {
+                                                           const __grid_constant__ GatherRows g) {
     const int64_t row = blockIdx.x;
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
     const int nvec = K >> 3;

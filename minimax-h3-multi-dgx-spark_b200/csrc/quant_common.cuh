@@ -6,8 +6,10 @@
 // and |fl(x/s) - x/s| <= 2^-18 for |x/s| <= 128, so |t - fl(x/s)| < 2^-15.
 // Whenever t is farther than 2^-14 from the half-integer between its two
 // neighbouring integers, rint(t) == rint(fl(x/s)); only inside that window
-// (about 1 element in 16k for smooth data) the exact division is done.
-// Everything per element runs on the FMA/ALU pipes (no conversion-unit op).
+// (about 1 element in 16k for smooth data; the 8 elements of a group are then
+// redone together) the exact division is done.  Everything per element runs
+// on the FMA/ALU pipes (no conversion-unit op), two elements per fp32
+// instruction.
 #pragma once
 
 #include "common.cuh"
@@ -19,28 +21,63 @@ namespace h3b {
 // The low byte of the sum's bit pattern is the two's-complement low byte of
 // that integer, because 0x4B400000 has a zero low byte.
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kNearHalf = 0.5f - 6.103515625e-05f;  // 0.5 - 2^-14
 
-// One element -> its int8 code in the low byte of the returned word.
-__device__ __forceinline__ uint32_t quant1(float x, float s, float r) {
-    const float t = __fmul_rn(x, r);
-    const float m = __fadd_rn(t, kRoundMagic);
-    const float n = __fsub_rn(m, kRoundMagic);
-    if (fabsf(__fsub_rn(t, n)) > 0.5f - 6.103515625e-05f /* 2^-14 */) {
-        // within reach of a half-integer: decide with the exact quotient
-        const float e = __fadd_rn(__fdiv_rn(x, s), kRoundMagic);
-        return __float_as_uint(e);
-    }
-    // |t| <= 127 by construction (|x| <= absmax), so the clamp to [-127, 127]
-    // of the reference formula never changes a code
-    return __float_as_uint(m);
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction per two lanes'
+// worth of IEEE round-to-nearest results, identical to the scalar ops).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
-// 8 values -> 8 int8 codes packed into two 32-bit words (s == 0 gives zeros)
+// 8 values -> 8 int8 codes packed into two 32-bit words (s == 0 gives zeros).
+// Fast path for all 8: t = x * r, m = t + magic (code in m's low byte),
+// d = t - (m - magic).  If any |d| is not below 0.5 - 2^-14 (t near a
+// half-integer, or NaN: r = inf for a subnormal scale), the 8 elements are
+// redone with the exact division.
 __device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, float r) {
     if (s == 0.0f) return make_uint2(0u, 0u);
+    const uint64_t rr = f2(r, r), mg = f2(kRoundMagic, kRoundMagic);
     uint32_t c[8];
+    bool near = false;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) c[e] = quant1(v[e], s, r);
+    for (int e = 0; e < 4; ++e) {
+        const uint64_t t = mul2(f2(v[2 * e], v[2 * e + 1]), rr);
+        const uint64_t m = add2(t, mg);
+        const uint64_t d = sub2(t, sub2(m, mg));
+        float m0, m1, d0, d1;
+        f2_split(m, m0, m1);
+        f2_split(d, d0, d1);
+        c[2 * e] = __float_as_uint(m0);
+        c[2 * e + 1] = __float_as_uint(m1);
+        near |= !(fabsf(d0) <= kNearHalf) | !(fabsf(d1) <= kNearHalf);
+    }
+    if (near) {
+        // rare: decide every element of the group with the exact quotient
+#pragma unroll
+        for (int e = 0; e < 8; ++e) c[e] = __float_as_uint(__fadd_rn(__fdiv_rn(v[e], s), kRoundMagic));
+    }
+    // |fl(x/s)| <= 127 by construction (|x| <= absmax), so the clamp to
+    // [-127, 127] of the reference formula never changes a code
     const uint32_t a = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
     const uint32_t b = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
     return make_uint2(a, b);

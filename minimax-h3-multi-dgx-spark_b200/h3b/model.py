@@ -9,9 +9,9 @@ configurations use a random-init stand-in with the same block structure:
       h = gate_norm_mod_(x, o, ga, w2, eps, ridx, s1m, shm)
       o = mlp(h)                            up INT8 linear -> GELU(tanh) -> down INT8 linear
       gate_(x, o, gm, ridx)
-  (with FUSED_PRODUCERS the norm kernels also quantise their output for the
-  INT8 linear they feed, and the GELU runs inside the down projection's
-  quantiser)
+  (with FUSED_NORM_QUANT the norm kernels also quantise their output for the
+  INT8 linear they feed; with FUSED_GELU_QUANT the GELU runs inside the down
+  projection's quantiser)
   sp_attention: qkv INT8 linear -> Ulysses forward all-to-all (q, k, v) ->
       SDPA over [1, H/P, S, Dh] -> inverse all-to-all -> out INT8 linear.
 
@@ -183,15 +183,18 @@ FUSED_EXCHANGE = os.environ.get("H3B_FUSED_EXCHANGE", "1") != "0"
 
 # The modulated activations feed only INT8 linears, so the norm kernels can emit
 # their int8 codes and scales directly (norm_mod_quant / gate_norm_mod_quant_)
-# and the GELU can run inside the down projection's quantiser; results equal the
-# unfused sequence bit for bit.  The unfused kernels are faster today (the fused
-# ones are latency-bound at their register footprint), so they are the default.
-FUSED_PRODUCERS = False
+# and the GELU can run inside the down projection's quantiser (gelu_quant);
+# results equal the unfused sequence bit for bit.  Each is switchable
+# (H3B_FUSED_NORM_QUANT, H3B_FUSED_GELU_QUANT = 0 / 1); the defaults are the
+# faster form as measured in the block.
+FUSED_NORM_QUANT = os.environ.get("H3B_FUSED_NORM_QUANT", "0") == "1"
+FUSED_GELU_QUANT = os.environ.get("H3B_FUSED_GELU_QUANT", "0") == "1"
 
 
 def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, overlap_groups=None):
     """One fused DiT block on the rank's rows x [s_local, D] (updated in place and returned)."""
-    fused = FUSED_PRODUCERS if fused_producers is None else fused_producers
+    fused = FUSED_NORM_QUANT if fused_producers is None else fused_producers
+    fused_gelu = FUSED_GELU_QUANT if fused_producers is None else fused_producers
     s1a, sha, ga, s1m, shm, gm = p.tables
     if fused:
         hq = fuse.norm_mod_quant(x, p.n1w, cfg.eps, ridx, s1a, sha)
@@ -208,7 +211,7 @@ def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, ov
     del o
     u = _lin_q(hq, p.up)
     del hq
-    aq = _gelu_quant(u) if fused else _quant(F.gelu(u, approximate="tanh"))
+    aq = _gelu_quant(u) if fused_gelu else _quant(F.gelu(u, approximate="tanh"))
     del u
     m = _lin_q(aq, p.down)
     del aq

@@ -32,6 +32,10 @@ def test_quant_bit_exact(M, K):
     x[0] = 0  # all-zero row: scale 0, codes 0
     if M > 2:
         x[2, 5] = 1e4  # one outlier dominates the row's scale
+    if M > 4:
+        # tiny rows: subnormal scales (1/s overflows to inf) and subnormal elements
+        x[3] = (randn_bf16((K,), seed=M + 1).float() * 1e-39).to(torch.bfloat16)
+        x[4] = (randn_bf16((K,), seed=M + 2).float() * 1e-36).to(torch.bfloat16)
     q_ref, s_ref = oracle.quant_rowwise(bits(x))
     xq, xs = h3b.quant_rowwise(x.to(DEV))
     torch.cuda.synchronize()
