@@ -226,6 +226,15 @@ def seeded_rows(start, stop, dim, seed, dtype=torch.bfloat16):
 # ---------------------------------------------------------------------------
 # DiT block / step workload
 
+def gemm_shapes(cfg, s_local, world, exchange):
+    """(M, N, K) of the launches the "gemm" span covers in one block: out, up and
+    down always; qkv too unless it runs as the fused GEMM + exchange (its own span)."""
+    from h3b import model as hm
+    shapes = [(s_local, cfg.dim, cfg.dim), (s_local, cfg.ffn, cfg.dim), (s_local, cfg.dim, cfg.ffn)]
+    fused_qkv = world > 1 and exchange == "p2p" and hm.FUSED_EXCHANGE and overlap_groups(cfg, world) == 0
+    return shapes if fused_qkv else [(s_local, 3 * cfg.dim, cfg.dim)] + shapes
+
+
 def overlap_groups(cfg, world):
     """Head groups the block's attention uses (0: exchange and attention in sequence)."""
     if world == 1:
@@ -320,34 +329,48 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
 
 
 def gemm_dram_traffic(shapes):
-    """DRAM bytes per GEMM launch: algorithmic bytes (A + B + bf16 out + scales + bias) of
-    the step's launches, scaled by the DRAM/algorithmic ratio of the ncu capture in
-    profiles/ncu_traffic.json (a smaller case of the same kernel; its traffic is
-    operand + output bytes, which grow in proportion)."""
+    """DRAM bytes per GEMM launch, averaged over the step's launches: each shape's
+    algorithmic bytes (A + B + bf16 out + scales + bias) times the DRAM/algorithmic
+    ratio that profiles/ncu_traffic.json records for its (N, K) from an ncu capture
+    of a smaller M (the operand, re-read and output bytes all grow in proportion
+    to M); shapes without a recorded ratio use the "default" entry."""
     try:
         with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
-            ratio = json.load(f)["gemm_i8_kernel"]["ratio"]
-    except (OSError, ValueError, KeyError):
+            rec = json.load(f)
+    except (OSError, ValueError):
         return None, None
-    algo = [M * K + N * K + 2 * M * N + 4 * M + 6 * N for M, N, K in shapes]
-    return ratio * sum(algo) / len(algo), ratio
+    ratios = {tuple(e["nk"]): e["ratio"] for e in rec.get("shapes", [])}
+    default = rec.get("default", {}).get("ratio")
+    total, used = 0.0, []
+    for M, N, K in shapes:
+        r = ratios.get((N, K), default)
+        if r is None:
+            return None, None
+        used.append(round(r, 3))
+        total += r * (M * K + N * K + 2 * M * N + 4 * M + 6 * N)
+    return total / len(shapes), used
 
 
-def gemm_roofline(spans, pk, src, shapes=None):
+def gemm_roofline(spans, pk, src, shapes=None, in_step=False):
+    """Roofline of the INT8 GEMM launches of the timed region.  Peak: 2 x the
+    measured dense bf16 rate (kind::i8 issues at twice kind::f16), the sustained
+    figure for launches timed inside a long step (power-capped clocks), the burst
+    figure for a GEMM timed alone."""
     g = spans.get("gemm")
     if not g or g["ms"] <= 0:
         return None
     achieved = g["work"] / (g["ms"] * 1e-3) / 1e12  # TOPS
-    peak = 2.0 * pk["bf16_tflops"]
-    traffic, ratio = gemm_dram_traffic(shapes) if shapes else (None, None)
+    key = "bf16_tflops_sustained" if in_step else "bf16_tflops"
+    peak = 2.0 * pk[key]
+    traffic, ratios = gemm_dram_traffic(shapes) if shapes else (None, None)
     return {"kernel": "gemm_i8_pair_kernel (tcgen05 cta_group::2 kind::i8 + dequant epilogue)", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
             "frac": round(achieved / peak, 4), "traffic": None if traffic is None else int(traffic),
-            "traffic_note": None if ratio is None else
-            f"bytes per launch: algorithmic operand+output bytes x {ratio:.3f} (DRAM/algorithmic of the ncu "
-            "capture in profiles/gemm_i8_pair_linear_m32768.md)",
-            "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TFLOP/s burst; kind::i8 issues at "
-                           "twice the kind::f16 rate on B200)",
+            "traffic_note": None if ratios is None else
+            f"bytes per launch (mean over the step's shapes): algorithmic operand+output bytes x the DRAM/algorithmic "
+            f"ratio per (N, K) from profiles/ncu_traffic.json ({ratios})",
+            "peak_source": f"2 x {src} bf16 dense, {'sustained' if in_step else 'burst'} ({pk[key]} TFLOP/s; "
+                           "kind::i8 issues at twice the kind::f16 rate on B200)",
             "work_per_step": g["work"], "launches_per_step": g["calls"], "ms_per_step": round(g["ms"], 3)}
 
 
@@ -599,8 +622,8 @@ def main():
                                "parallelism": f"ulysses_sp{world}", "exchange": args.exchange if world > 1 else None,
                                "overlap_groups": overlap_groups(cfg, world),
                                "l2": "inputs larger than L2 (no flush)"},
-                    "roofline": gemm_roofline(spans, pk, pk_src, [(s_local, 3 * cfg.dim, cfg.dim), (s_local, cfg.dim, cfg.dim),
-                                                                  (s_local, cfg.ffn, cfg.dim), (s_local, cfg.dim, cfg.ffn)]),
+                    "roofline": gemm_roofline(spans, pk, pk_src, gemm_shapes(cfg, s_local, world, args.exchange),
+                                              in_step=True),
                     "clocks": clocks, "e2e": e2e,
                     "gpu_launches": int(round(launches * args.steps)), "breakdown": breakdown(spans, pk)}
             if rank == 0 and world == 1 and not args.no_cpu_baseline and not step_cfg:
