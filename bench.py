@@ -65,6 +65,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a"],
                     default="dit_block")
     ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
+    ap.add_argument("--convrot", type=int, default=0, choices=[0, 64, 256],
+                    help="linear workload: ConvRot quantiser with this rotation group (0 = plain)")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
     ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
     ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / S of the fused workload")
@@ -478,7 +480,7 @@ def linear_workload(args, dev):
 
     def step():
         flush.zero_()
-        h3b.linear(x, w, ws, b)
+        h3b.linear(x, w, ws, b, convrot_group=args.convrot)
 
     ms, clocks = timed(step, args.steps, args.warmup, 1, dev)
     with Trace() as tr:
@@ -635,7 +637,8 @@ def main():
             line = {"metric": "INT8 linear (config 0) TOPS", "value": round(2 * M * 5120 * 5120 / (ms * 1e-3) / 1e12, 1),
                     "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
-                    "config": {"workload": "linear", "M": M, "N": 5120, "K": 5120, "l2": "256 MB flush per step"},
+                    "config": {"workload": "linear", "M": M, "N": 5120, "K": 5120, "convrot_group": args.convrot,
+                               "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
         elif args.workload == "qkv_a2a":

@@ -68,6 +68,21 @@ H3B_API int h3b_status_clear(void *stream);
  * the plain per-token absmax quantiser; the ConvRot rotation is not applied). */
 H3B_API int h3b_quant_rowwise(const void *x, int64_t ldx, int64_t M, int64_t K, int8_t *xq, float *xs, void *stream);
 
+/* The quantiser with the ConvRot rotation: every group of `group` columns
+ * (64 or 256; K % group == 0, K <= 32768) of row m is rotated by the normalised
+ * Walsh-Hadamard transform y = H x / sqrt(group) (Sylvester order, computed as
+ * the fast transform in fp32: stages h = 1, 2, .., group/2, each pair
+ * (y_i + y_{i+h}, y_i - y_{i+h}) rounded once, then the exact scale), and y
+ * is quantised as by h3b_quant_rowwise: xs[m] = max|y| / 127, xq = rint(y / xs).
+ * The weights of such a linear are stored rotated the same way.  Replaces
+ * comfy-kitchen 0.2.39's _C.quantize_int8_rowwise_convrot64(x, xq, xs, 256, ...)
+ * at comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:89-95 (input_act
+ * none); that kernel's source is not part of the reference, so its exact
+ * arithmetic is not pinned -- this is the rotate-then-quantise scheme it
+ * names, with the rounding defined above. */
+H3B_API int h3b_quant_rowwise_convrot(const void *x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t *xq,
+                                      float *xs, void *stream);
+
 /* GELU (tanh approximation, PyTorch's fp32 formula) fused into the quantiser:
  * the codes / scales of bf16(gelu(u)) for u bf16 [M,K] (leading dimension ldu)
  * -- the input of the FFN down projection -- without writing the activation.

@@ -13,6 +13,10 @@
 // quant(F.gelu(u, approximate="tanh")) bit for bit without the bf16 GELU output
 // ever reaching HBM.
 //
+// ConvRot variant (quant_convrot_kernel): the rows are first rotated group by
+// group with the Walsh-Hadamard transform, as the reference's fast path does
+// before quantising (its weights are stored rotated the same way).
+//
 // Gather variant (the inverse Ulysses exchange fused with the quantiser of the
 // attention output projection): row m is assembled from every rank's attention
 // output rows, read over NVLink from the peers' buffers, so the exchanged rows
@@ -105,6 +109,115 @@ __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __res
     }
 }
 
+// ConvRot variant: each group of G columns (G = 64 or 256) of the row is rotated
+// by the normalised Walsh-Hadamard transform before the absmax and the codes
+// (y = H_G x / sqrt(G), Sylvester order).  Fast transform in binary32, stages
+// h = 1, 2, 4 inside a thread's 8-element vector, then h = 8 .. G/2 across the
+// G/8 lanes holding the group (lane ^ h/8 is the partner: the group's vectors
+// sit in consecutive lanes because NT % (G/8) == 0), then the exact scale by
+// 1/sqrt(G); two elements per f32x2 instruction.  Every lane runs every
+// shuffle (lanes past the row's end carry zeros), so the full-warp shuffles
+// never see an exited lane.
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t shfl_xor2(uint64_t v, int m) {
+    return __shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
+}
+
+template <int VPT, int NT, int G>
+__global__ void __launch_bounds__(NT) quant_convrot_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
+                                                           int8_t* __restrict__ xq, float* __restrict__ xs) {
+    constexpr int LG = G / 8;  // lanes per group
+    constexpr float kInv = G == 64 ? 0.125f : 0.0625f;
+    static_assert(G == 64 || G == 256, "rotation groups of 64 or 256 columns");
+    const int64_t row = blockIdx.x;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+    const int nvec = K >> 3;
+    const int lane = threadIdx.x & 31;
+    // p[i][k] holds elements 2k, 2k+1 of vector i as an fp32 pair (f32x2 arithmetic)
+    uint64_t p[VPT][4];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int j = threadIdx.x + i * NT;
+        const uint4 v = j < nvec ? xr[j] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        // stage h = 1: pairs (2k, 2k+1) inside one word
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float a = bf16_lo(w[k]), b = bf16_hi(w[k]);
+            p[i][k] = f2(__fadd_rn(a, b), __fsub_rn(a, b));
+        }
+        // h = 2: pairs (p0, p1), (p2, p3); h = 4: (p0, p2), (p1, p3)
+        uint64_t t0 = add2(p[i][0], p[i][1]), t1 = sub2(p[i][0], p[i][1]);
+        uint64_t t2 = add2(p[i][2], p[i][3]), t3 = sub2(p[i][2], p[i][3]);
+        p[i][0] = add2(t0, t2);
+        p[i][2] = sub2(t0, t2);
+        p[i][1] = add2(t1, t3);
+        p[i][3] = sub2(t1, t3);
+    }
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        // h = 8 .. G/2 across lanes: the lower partner takes mine + theirs, the
+        // upper theirs - mine, i.e. theirs + s * mine with s = +-1 (exact product,
+        // one rounding: bit-identical to the add / subtract)
+#pragma unroll
+        for (int sh = 1; sh < LG; sh <<= 1) {
+            const float sg = (lane & sh) ? -1.0f : 1.0f;
+            const uint64_t s2 = f2(sg, sg);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) p[i][k] = fma2(s2, p[i][k], shfl_xor2(p[i][k], sh));
+        }
+        const uint64_t inv2 = f2(kInv, kInv);
+        const int j = threadIdx.x + i * NT;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            p[i][k] = mul2(p[i][k], inv2);
+            float a, b;
+            f2_split(p[i][k], a, b);
+            if (j < nvec) m = max(m, max(__float_as_uint(a) & 0x7FFFFFFFu, __float_as_uint(b) & 0x7FFFFFFFu));
+        }
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    __shared__ uint32_t wmax[NT / 32];
+    if (lane == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = wmax[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w) m = max(m, wmax[w]);
+    float s, r;
+    row_scale(__uint_as_float(m), s, r);
+    if (threadIdx.x == 0) xs[row] = s;
+    uint2* qr = reinterpret_cast<uint2*>(xq + row * (int64_t)K);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int j = threadIdx.x + i * NT;
+        if (j < nvec) {
+            float f[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) f2_split(p[i][k], f[2 * k], f[2 * k + 1]);
+            qr[j] = quant8(f, s, r);
+        }
+    }
+}
+
+template <int NT, int G>
+static void launch_convrot(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
+                           cudaStream_t s) {
+    dim3 grid((unsigned)M), block(NT);
+    switch (vpt) {
+#define H3B_RCASE(V) \
+    case V: quant_convrot_kernel<V, NT, G><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
+        H3B_RCASE(1) H3B_RCASE(2) H3B_RCASE(3) H3B_RCASE(4) H3B_RCASE(5) H3B_RCASE(6) H3B_RCASE(7) H3B_RCASE(8)
+        H3B_RCASE(10) H3B_RCASE(12) H3B_RCASE(14) H3B_RCASE(16)
+#undef H3B_RCASE
+        default: break;
+    }
+}
+
 template <int NT, Act ACT, bool GATHER = false>
 static void launch_quant(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
                          cudaStream_t s, GatherRows g = GatherRows{}) {
@@ -151,6 +264,32 @@ static int quant_impl(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* 
 
 int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs, cudaStream_t s) {
     return quant_impl<Act::kNone>(x, ldx, M, K, xq, xs, s, "h3b_quant_rowwise");
+}
+
+static int quant_convrot(const void* x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t* xq, float* xs,
+                         cudaStream_t s) {
+    const char* who = "h3b_quant_rowwise_convrot";
+    H3B_REQUIRE(x && xq && xs, "%s: NULL pointer", who);
+    H3B_REQUIRE(group == 64 || group == 256, "%s: group=%lld (64 or 256 supported)", who, (long long)group);
+    H3B_REQUIRE(M >= 0 && M < (1ll << 31) && K > 0 && K % group == 0 && K <= 32768,
+                "%s: K=%lld must be a positive multiple of the group (%lld), <= 32768", who, (long long)K,
+                (long long)group);
+    H3B_REQUIRE(ldx >= K && ldx % 8 == 0 && aligned(x, 16), "%s: x must be 16-byte aligned with ldx %% 8 == 0", who);
+    H3B_REQUIRE(aligned(xq, 8), "%s: xq must be 8-byte aligned", who);
+    if (M == 0) return H3B_OK;
+    const int nvec = (int)(K / 8);
+    const uint16_t* xp = static_cast<const uint16_t*>(x);
+    int vpt = pick_vpt((nvec + 127) / 128);
+    if (vpt > 0) {
+        if (group == 256) launch_convrot<128, 256>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        else launch_convrot<128, 64>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+    } else {
+        vpt = pick_vpt((nvec + 255) / 256);
+        if (group == 256) launch_convrot<256, 256>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        else launch_convrot<256, 64>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+    }
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
 }
 
 static int gather_quant(const void* const* src, int64_t src_ld, int64_t row_start, int64_t M, int64_t chunk_bytes,
@@ -201,4 +340,9 @@ extern "C" int h3b_gelu_quant(const void* u, int64_t ldu, int64_t M, int64_t K, 
 extern "C" int h3b_a2a_inv_quant(const void* const* src, int64_t src_ld, int64_t row_start, int64_t M,
                                  int64_t chunk_bytes, int world, int8_t* xq, float* xs, void* stream) {
     return h3b::gather_quant(src, src_ld, row_start, M, chunk_bytes, world, xq, xs, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_quant_rowwise_convrot(const void* x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t* xq,
+                                         float* xs, void* stream) {
+    return h3b::quant_convrot(x, ldx, M, K, group, xq, xs, static_cast<cudaStream_t>(stream));
 }

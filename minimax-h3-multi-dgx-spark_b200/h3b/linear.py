@@ -1,6 +1,7 @@
 """INT8 linear ops (activation quantiser, GEMM + dequant, patched Linear) over libh3b.
 
 Mirrors the reference's operator surface:
+  quant_rowwise / quant_rowwise_convrot      the quantiser called at h3_linear_fast_patch.py:89-95
   int8_mm_scaled(xq, w, xs, ws, out=None)    comfyui_nodes/h3-linear-fast/int8_gemm_triton.py:74-83
   supported(K)                               int8_gemm_triton.py:86-87
   int8_linear(x, weight, weight_scale, ...)  the patched comfy_kitchen int8_linear,
@@ -34,6 +35,25 @@ def quant_rowwise(x, xq=None, xs=None):
         xs = torch.empty((M, 1), dtype=torch.float32, device=x.device)
     with span("quant", 3 * M * K + 4 * M):
         check(lib.h3b_quant_rowwise(ptr(x), x.stride(0), M, K, ptr(xq), ptr(xs), stream_of(x)), "h3b_quant_rowwise")
+    return xq, xs
+
+
+def quant_rowwise_convrot(x, group=256, xq=None, xs=None):
+    """quant_rowwise of the ConvRot-rotated rows: each group of `group` (64 or 256)
+    columns rotated by the normalised Walsh-Hadamard transform first
+    (h3b_quant_rowwise_convrot; the quantiser of the reference's fast path,
+    h3_linear_fast_patch.py:89-95)."""
+    require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("quant_rowwise_convrot: x must be a 2-D bf16 tensor with unit column stride")
+    M, K = x.shape
+    if xq is None:
+        xq = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    if xs is None:
+        xs = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    with span("quant_convrot", 3 * M * K + 4 * M):
+        check(lib.h3b_quant_rowwise_convrot(ptr(x), x.stride(0), M, K, group, ptr(xq), ptr(xs), stream_of(x)),
+              "h3b_quant_rowwise_convrot")
     return xq, xs
 
 
@@ -118,13 +138,14 @@ def int8_mm_i32(xq, w, out=None):
     return out
 
 
-def linear(x, w, ws, bias=None):
-    """The INT8 linear on a [*, K] bf16 activation: per-token quant + GEMM + dequant(+bias)."""
+def linear(x, w, ws, bias=None, convrot_group=0):
+    """The INT8 linear on a [*, K] bf16 activation: per-token quant + GEMM + dequant(+bias).
+    convrot_group (64 / 256): the ConvRot quantiser, for weights stored rotated."""
     kin = x.shape[-1]
     x2d = x.reshape(-1, kin)
     if not x2d.is_contiguous():
         x2d = x2d.contiguous()
-    xq, xs = quant_rowwise(x2d)
+    xq, xs = quant_rowwise_convrot(x2d, convrot_group) if convrot_group else quant_rowwise(x2d)
     out = int8_mm_scaled(xq, w, xs, ws, bias=bias)
     return out if x.dim() == 2 else out.reshape(*x.shape[:-1], w.shape[0])
 
@@ -133,16 +154,20 @@ def int8_linear(x, weight, weight_scale, bias=None, out_dtype=None, convrot=Fals
                 input_act=None, input_act_weight=None, input_act_eps=0.0, residual=None, residual_scale=None):
     """Signature of comfy_kitchen.backends.cuda.int8_linear (h3_linear_fast_patch.py:60-61).
 
-    Covers the plain per-token quantiser (convrot=False), no input activation and
-    no residual; anything else raises NotImplementedError so that an installer
-    can route the call to the original implementation, as the reference does
-    for ineligible calls (h3_linear_fast_patch.py:64-80)."""
-    if convrot or input_act not in (None, "none") or residual is not None:
-        raise NotImplementedError("h3b int8_linear: convrot / input_act / residual variants are not covered")
+    Covers the plain per-token quantiser (convrot=False) and the ConvRot one
+    (convrot=True, convrot_groupsize 64 or 256 -- the reference's fast path
+    takes 256 only, :64), with no input activation and no residual; anything
+    else raises NotImplementedError so that an installer can route the call to
+    the original implementation, as the reference does for ineligible calls
+    (h3_linear_fast_patch.py:64-80)."""
+    if input_act not in (None, "none") or residual is not None:
+        raise NotImplementedError("h3b int8_linear: input_act / residual variants are not covered")
+    if convrot and convrot_groupsize not in (64, 256):
+        raise NotImplementedError(f"h3b int8_linear: ConvRot group {convrot_groupsize} (64 or 256 covered)")
     if (out_dtype or x.dtype) != torch.bfloat16 or x.dtype != torch.bfloat16:
         raise NotImplementedError("h3b int8_linear: bf16 in/out only")
     n = weight.shape[0]
     ws = weight_scale.reshape(-1).to(torch.float32)
     if ws.numel() != n:
         ws = ws.expand(n).contiguous()
-    return linear(x, weight.contiguous(), ws, bias)
+    return linear(x, weight.contiguous(), ws, bias, convrot_group=convrot_groupsize if convrot else 0)

@@ -36,6 +36,10 @@ def lib():
         p, i64, f32, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int
         L.h3o_quant_rowwise.argtypes = [p, i64, i64, p, p]
         L.h3o_quant_rowwise.restype = None
+        L.h3o_quant_rowwise_convrot.argtypes = [p, i64, i64, i64, p, p, p]
+        L.h3o_quant_rowwise_convrot.restype = None
+        L.h3o_rotate_groups.argtypes = [p, i64, i64, p]
+        L.h3o_rotate_groups.restype = None
         L.h3o_int8_mm_scaled.argtypes = [p, p, p, p, p, i64, i64, i64, p, p, i32]
         L.h3o_int8_mm_scaled.restype = None
         L.h3o_row_sumsq.argtypes = [p, i64, i32]
@@ -95,6 +99,28 @@ def quant_rowwise(x_bf16):
     q = np.empty((M, K), np.int8)
     s = np.empty(M, np.float32)
     lib().h3o_quant_rowwise(_ptr(x), M, K, _ptr(q), _ptr(s))
+    return q, s
+
+
+def rotate_groups(x_bf16, group=256):
+    """x [M,K] bf16 bits -> fp32 [M,K]: each group of `group` columns rotated by
+    the normalised Walsh-Hadamard transform (h3o_rotate_groups)."""
+    x = _c(x_bf16, np.uint16)
+    M, K = x.shape
+    y = np.empty((M, K), np.float32)
+    for m in range(M):
+        lib().h3o_rotate_groups(_ptr(x[m]), K, group, _ptr(y[m]))
+    return y
+
+
+def quant_rowwise_convrot(x_bf16, group=256):
+    """x [M,K] bf16 bits -> (q [M,K] int8, s [M] float32) of the ConvRot-rotated rows."""
+    x = _c(x_bf16, np.uint16)
+    M, K = x.shape
+    q = np.empty((M, K), np.int8)
+    s = np.empty(M, np.float32)
+    work = np.empty(K, np.float32)
+    lib().h3o_quant_rowwise_convrot(_ptr(x), M, K, group, _ptr(q), _ptr(s), _ptr(work))
     return q, s
 
 

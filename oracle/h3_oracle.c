@@ -117,6 +117,63 @@ void h3o_quant_rowwise(const uint16_t *x, int64_t M, int64_t K, int8_t *q, float
 }
 
 /* ------------------------------------------------------------------------- */
+/* a1 with the ConvRot rotation (the quantiser of the reference's fast path,
+ * comfy-kitchen 0.2.39 _C.quantize_int8_rowwise_convrot64(x, xq, xs, 256, ...),
+ * called at comfyui_nodes/h3-linear-fast/h3_linear_fast_patch.py:89-95; its
+ * source is not part of the reference, so this restates the published
+ * rotate-then-quantise scheme and the exact arithmetic is this file's
+ * definition -- parity against comfy-kitchen itself is unpinned):
+ *   each group of G consecutive columns (G = 64 or 256, a power of 4) is
+ *   rotated by the normalised Walsh-Hadamard matrix, y = H_G x / sqrt(G)
+ *   (Sylvester order), as the fast transform in binary32: stages h = 1, 2, 4,
+ *   .., G/2 in that order, each pair (i, i+h) with (i & h) == 0 becoming
+ *   (y_i + y_{i+h}, y_i - y_{i+h}) with one rounding each, then a multiply by
+ *   1/sqrt(G) (a power of two: exact unless the value is subnormal);
+ *   the rotated row is then quantised as h3o_quant_rowwise does, from its
+ *   binary32 values: s = absmax / 127, q = clamp(rint(y / s), -127, 127).
+ * The weights of such a linear are stored rotated the same way (W' = W H / sqrt(G)),
+ * so x W^T = (x H)(W H)^T / G up to the quantisation. */
+void h3o_rotate_groups(const uint16_t *x, int64_t K, int64_t G, float *y) {
+    const float inv = G == 64 ? 0.125f : (G == 256 ? 0.0625f : 1.0f / sqrtf((float)G));
+    for (int64_t k = 0; k < K; ++k) y[k] = bf2f(x[k]);
+    for (int64_t g0 = 0; g0 < K; g0 += G) {
+        float *v = y + g0;
+        for (int64_t h = 1; h < G; h <<= 1)
+            for (int64_t i = 0; i < G; ++i)
+                if ((i & h) == 0) {
+                    const float a = v[i], b = v[i + h];
+                    v[i] = a + b;
+                    v[i + h] = a - b;
+                }
+        for (int64_t i = 0; i < G; ++i) v[i] = v[i] * inv;
+    }
+}
+
+void h3o_quant_rowwise_convrot(const uint16_t *x, int64_t M, int64_t K, int64_t G, int8_t *q, float *s, float *work) {
+    for (int64_t m = 0; m < M; ++m) {
+        h3o_rotate_groups(x + m * K, K, G, work);
+        float amax = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float a = fabsf(work[k]);
+            if (a > amax) amax = a;
+        }
+        const float sc = amax / 127.0f;
+        s[m] = sc;
+        int8_t *qr = q + m * K;
+        if (sc == 0.0f) {
+            memset(qr, 0, (size_t)K);
+            continue;
+        }
+        for (int64_t k = 0; k < K; ++k) {
+            float r = nearbyintf(work[k] / sc);
+            if (r > 127.0f) r = 127.0f;
+            if (r < -127.0f) r = -127.0f;
+            qr[k] = (int8_t)r;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------- */
 /* a2: int8 x int8 -> int32 GEMM with the fp32 dequant epilogue.
  * acc[m,n] = sum_k xq[m,k] * w[n,k]                (int32, exact)
  * y[m,n]   = bf16((float(acc) * xs[m]) * ws[n])     int8_gemm_triton.py:2,61-66

@@ -152,3 +152,38 @@ def test_quant_half_integer_ties():
     torch.cuda.synchronize()
     np.testing.assert_array_equal(xq.cpu().numpy(), q_ref)
     np.testing.assert_array_equal(xs.cpu().numpy().reshape(-1), s_ref)
+
+
+@pytest.mark.parametrize("M,K,group", [(37, 5120, 256), (4096, 5120, 256), (129, 13824, 256), (64, 256, 256),
+                                       (300, 1024, 64), (5, 64, 64), (3, 32768, 256)])
+def test_quant_convrot_bit_exact(M, K, group):
+    """ConvRot quantiser (group-wise Walsh-Hadamard rotation, then absmax codes)
+    against the C restatement, bit for bit; zero, outlier and tiny rows."""
+    x = randn_bf16((M, K), seed=M * 5 + K + group)
+    x[0] = 0
+    if M > 2:
+        x[2, 7] = 3e3
+    if M > 4:
+        x[3] = (randn_bf16((K,), seed=M + 11).float() * 1e-38).to(torch.bfloat16)
+        x[4] = torch.randint(-8, 9, (K,), generator=gen(M)).to(torch.bfloat16)  # exact rotation, many ties
+    q_ref, s_ref = oracle.quant_rowwise_convrot(bits(x), group)
+    xq, xs = h3b.quant_rowwise_convrot(x.to(DEV), group)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(xs.cpu().numpy().reshape(-1), s_ref)
+    np.testing.assert_array_equal(xq.cpu().numpy(), q_ref)
+
+
+def test_int8_linear_convrot_vs_oracle():
+    """The patched int8_linear with convrot=True (the reference fast path's case):
+    rotated quantiser + GEMM + dequant equals the oracle on a row sample; an
+    unsupported group size raises NotImplementedError (the caller's fallback)."""
+    M, N, K = 2048, 1536, 5120
+    x = randn_bf16((M, K), seed=21)
+    w, ws, _ = _weights(N, K, seed=22)
+    y = h3b.int8_linear(x.to(DEV), w.to(DEV), ws.to(DEV), None, torch.bfloat16, convrot=True, convrot_groupsize=256)
+    torch.cuda.synchronize()
+    rows = np.r_[0:32, 1000:1032, M - 32:M]
+    q, s = oracle.quant_rowwise_convrot(bits(x)[rows], 256)
+    np.testing.assert_array_equal(bits(y)[rows], oracle.int8_mm_scaled(q, w.numpy(), s, ws.numpy()))
+    with pytest.raises(NotImplementedError):
+        h3b.int8_linear(x[:, :K // 2].to(DEV), w[:, :K // 2].to(DEV), ws.to(DEV), convrot=True, convrot_groupsize=128)
