@@ -83,6 +83,19 @@ H3B_API int h3b_quant_rowwise(const void *x, int64_t ldx, int64_t M, int64_t K, 
 H3B_API int h3b_quant_rowwise_convrot(const void *x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t *xq,
                                       float *xs, void *stream);
 
+/* h3b_quant_rowwise_convrot with the SwiGLU input activation fused in front:
+ * x bf16 [M, 2K] (leading dimension ldx elements) holds the gate a = x[:, :K]
+ * and the up projection b = x[:, K:]; the row quantised is
+ * bf16(silu(a) * b), silu(a) = a / (1 + expf(-a)) in fp32 with one rounding
+ * per operation (equal to (F.silu(a.float()) * b.float()).to(bf16) in PyTorch),
+ * rotated and quantised exactly as h3b_quant_rowwise_convrot, without the
+ * activation reaching memory.  Replaces the reference fast path's fc2 call,
+ * _C.quantize_int8_rowwise_convrot64(..., input_act="swiglu"),
+ * h3_linear_fast_patch.py:63,89-95 (which half is the gate is not stated in
+ * the reference; the first half is the gate here). */
+H3B_API int h3b_swiglu_quant_convrot(const void *x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t *xq,
+                                     float *xs, void *stream);
+
 /* GELU (tanh approximation, PyTorch's fp32 formula) fused into the quantiser:
  * the codes / scales of bf16(gelu(u)) for u bf16 [M,K] (leading dimension ldu)
  * -- the input of the FFN down projection -- without writing the activation.

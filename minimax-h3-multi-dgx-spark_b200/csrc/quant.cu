@@ -127,7 +127,19 @@ __device__ __forceinline__ uint64_t shfl_xor2(uint64_t v, int m) {
     return __shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
 }
 
-template <int VPT, int NT, int G>
+// SwiGLU input activation (the fused "swiglu" input of the reference's second
+// FFN linear): the row holds 2K columns, gate a = x[:, :K], up b = x[:, K:];
+// the activation bf16(silu(a) * b), silu(a) = a / (1 + expf(-a)) in fp32 with
+// one rounding per operation (PyTorch's F.silu(a.float()) * b.float() cast to
+// bf16), then the rotation and the codes as for a plain bf16 input.
+__device__ __forceinline__ uint32_t swiglu2(uint32_t a, uint32_t b) {
+    const float a0 = bf16_lo(a), a1 = bf16_hi(a);
+    const float s0 = __fdiv_rn(a0, __fadd_rn(1.0f, expf(-a0)));
+    const float s1 = __fdiv_rn(a1, __fadd_rn(1.0f, expf(-a1)));
+    return pack_bf16x2(__fmul_rn(s0, bf16_lo(b)), __fmul_rn(s1, bf16_hi(b)));
+}
+
+template <int VPT, int NT, int G, bool SWIGLU = false>
 __global__ void __launch_bounds__(NT) quant_convrot_kernel(const uint16_t* __restrict__ x, int64_t ldx, int K,
                                                            int8_t* __restrict__ xq, float* __restrict__ xs) {
     constexpr int LG = G / 8;  // lanes per group
@@ -142,7 +154,11 @@ __global__ void __launch_bounds__(NT) quant_convrot_kernel(const uint16_t* __res
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         const int j = threadIdx.x + i * NT;
-        const uint4 v = j < nvec ? xr[j] : make_uint4(0u, 0u, 0u, 0u);
+        uint4 v = j < nvec ? xr[j] : make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (SWIGLU) {
+            const uint4 u = j < nvec ? xr[nvec + j] : make_uint4(0u, 0u, 0u, 0u);
+            v = make_uint4(swiglu2(v.x, u.x), swiglu2(v.y, u.y), swiglu2(v.z, u.z), swiglu2(v.w, u.w));
+        }
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         // stage h = 1: pairs (2k, 2k+1) inside one word
 #pragma unroll
@@ -204,13 +220,13 @@ __global__ void __launch_bounds__(NT) quant_convrot_kernel(const uint16_t* __res
     }
 }
 
-template <int NT, int G>
+template <int NT, int G, bool SWIGLU>
 static void launch_convrot(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
                            cudaStream_t s) {
     dim3 grid((unsigned)M), block(NT);
     switch (vpt) {
 #define H3B_RCASE(V) \
-    case V: quant_convrot_kernel<V, NT, G><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
+    case V: quant_convrot_kernel<V, NT, G, SWIGLU><<<grid, block, 0, s>>>(x, ldx, K, xq, xs); break;
         H3B_RCASE(1) H3B_RCASE(2) H3B_RCASE(3) H3B_RCASE(4) H3B_RCASE(5) H3B_RCASE(6) H3B_RCASE(7) H3B_RCASE(8)
         H3B_RCASE(10) H3B_RCASE(12) H3B_RCASE(14) H3B_RCASE(16)
 #undef H3B_RCASE
@@ -266,27 +282,29 @@ int quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, 
     return quant_impl<Act::kNone>(x, ldx, M, K, xq, xs, s, "h3b_quant_rowwise");
 }
 
+template <bool SWIGLU>
 static int quant_convrot(const void* x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t* xq, float* xs,
-                         cudaStream_t s) {
-    const char* who = "h3b_quant_rowwise_convrot";
+                         cudaStream_t s, const char* who) {
     H3B_REQUIRE(x && xq && xs, "%s: NULL pointer", who);
     H3B_REQUIRE(group == 64 || group == 256, "%s: group=%lld (64 or 256 supported)", who, (long long)group);
     H3B_REQUIRE(M >= 0 && M < (1ll << 31) && K > 0 && K % group == 0 && K <= 32768,
                 "%s: K=%lld must be a positive multiple of the group (%lld), <= 32768", who, (long long)K,
                 (long long)group);
-    H3B_REQUIRE(ldx >= K && ldx % 8 == 0 && aligned(x, 16), "%s: x must be 16-byte aligned with ldx %% 8 == 0", who);
+    const int64_t row = SWIGLU ? 2 * K : K;
+    H3B_REQUIRE(ldx >= row && ldx % 8 == 0 && aligned(x, 16),
+                "%s: x must be 16-byte aligned with ldx >= %lld and ldx %% 8 == 0", who, (long long)row);
     H3B_REQUIRE(aligned(xq, 8), "%s: xq must be 8-byte aligned", who);
     if (M == 0) return H3B_OK;
     const int nvec = (int)(K / 8);
     const uint16_t* xp = static_cast<const uint16_t*>(x);
     int vpt = pick_vpt((nvec + 127) / 128);
     if (vpt > 0) {
-        if (group == 256) launch_convrot<128, 256>(vpt, xp, ldx, M, (int)K, xq, xs, s);
-        else launch_convrot<128, 64>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        if (group == 256) launch_convrot<128, 256, SWIGLU>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        else launch_convrot<128, 64, SWIGLU>(vpt, xp, ldx, M, (int)K, xq, xs, s);
     } else {
         vpt = pick_vpt((nvec + 255) / 256);
-        if (group == 256) launch_convrot<256, 256>(vpt, xp, ldx, M, (int)K, xq, xs, s);
-        else launch_convrot<256, 64>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        if (group == 256) launch_convrot<256, 256, SWIGLU>(vpt, xp, ldx, M, (int)K, xq, xs, s);
+        else launch_convrot<256, 64, SWIGLU>(vpt, xp, ldx, M, (int)K, xq, xs, s);
     }
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
@@ -344,5 +362,12 @@ extern "C" int h3b_a2a_inv_quant(const void* const* src, int64_t src_ld, int64_t
 
 extern "C" int h3b_quant_rowwise_convrot(const void* x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t* xq,
                                          float* xs, void* stream) {
-    return h3b::quant_convrot(x, ldx, M, K, group, xq, xs, static_cast<cudaStream_t>(stream));
+    return h3b::quant_convrot<false>(x, ldx, M, K, group, xq, xs, static_cast<cudaStream_t>(stream),
+                                     "h3b_quant_rowwise_convrot");
+}
+
+extern "C" int h3b_swiglu_quant_convrot(const void* x, int64_t ldx, int64_t M, int64_t K, int64_t group, int8_t* xq,
+                                        float* xs, void* stream) {
+    return h3b::quant_convrot<true>(x, ldx, M, K, group, xq, xs, static_cast<cudaStream_t>(stream),
+                                    "h3b_swiglu_quant_convrot");
 }

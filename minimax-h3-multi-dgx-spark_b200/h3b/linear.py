@@ -57,6 +57,24 @@ def quant_rowwise_convrot(x, group=256, xq=None, xs=None):
     return xq, xs
 
 
+def swiglu_quant_convrot(x, group=256, xq=None, xs=None):
+    """quant_rowwise_convrot(bf16(silu(x[:, :K]) * x[:, K:])) for x bf16 [M, 2K]
+    without materialising the activation (h3b_swiglu_quant_convrot; the
+    reference fast path's input_act="swiglu", h3_linear_fast_patch.py:63,93-95)."""
+    require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1 or x.shape[1] % 2:
+        raise ValueError("swiglu_quant_convrot: x must be a 2-D bf16 [M, 2K] tensor with unit column stride")
+    M, K = x.shape[0], x.shape[1] // 2
+    if xq is None:
+        xq = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    if xs is None:
+        xs = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    with span("swiglu_quant_convrot", 5 * M * K + 4 * M):
+        check(lib.h3b_swiglu_quant_convrot(ptr(x), x.stride(0), M, K, group, ptr(xq), ptr(xs), stream_of(x)),
+              "h3b_swiglu_quant_convrot")
+    return xq, xs
+
+
 def gelu_quant(u, xq=None, xs=None):
     """quant_rowwise(F.gelu(u, approximate="tanh")) without materialising the GELU output."""
     require_cuda(u)
@@ -138,14 +156,21 @@ def int8_mm_i32(xq, w, out=None):
     return out
 
 
-def linear(x, w, ws, bias=None, convrot_group=0):
+def linear(x, w, ws, bias=None, convrot_group=0, swiglu=False):
     """The INT8 linear on a [*, K] bf16 activation: per-token quant + GEMM + dequant(+bias).
-    convrot_group (64 / 256): the ConvRot quantiser, for weights stored rotated."""
+    convrot_group (64 / 256): the ConvRot quantiser, for weights stored rotated;
+    swiglu (with convrot_group): x is [*, 2K] and the quantised row is
+    bf16(silu(x[..., :K]) * x[..., K:])."""
     kin = x.shape[-1]
     x2d = x.reshape(-1, kin)
     if not x2d.is_contiguous():
         x2d = x2d.contiguous()
-    xq, xs = quant_rowwise_convrot(x2d, convrot_group) if convrot_group else quant_rowwise(x2d)
+    if swiglu:
+        if not convrot_group:
+            raise NotImplementedError("h3b linear: the SwiGLU input is covered with the ConvRot quantiser only")
+        xq, xs = swiglu_quant_convrot(x2d, convrot_group)
+    else:
+        xq, xs = quant_rowwise_convrot(x2d, convrot_group) if convrot_group else quant_rowwise(x2d)
     out = int8_mm_scaled(xq, w, xs, ws, bias=bias)
     return out if x.dim() == 2 else out.reshape(*x.shape[:-1], w.shape[0])
 
@@ -156,12 +181,16 @@ def int8_linear(x, weight, weight_scale, bias=None, out_dtype=None, convrot=Fals
 
     Covers the plain per-token quantiser (convrot=False) and the ConvRot one
     (convrot=True, convrot_groupsize 64 or 256 -- the reference's fast path
-    takes 256 only, :64), with no input activation and no residual; anything
-    else raises NotImplementedError so that an installer can route the call to
+    takes 256 only, :64), the latter also with the SwiGLU input activation
+    (input_act="swiglu", x [*, 2K]), bias optional, no residual -- every call
+    the reference's fast path accepts (:64-76); anything else raises
+    NotImplementedError so that an installer can route the call to
     the original implementation, as the reference does for ineligible calls
     (h3_linear_fast_patch.py:64-80)."""
-    if input_act not in (None, "none") or residual is not None:
-        raise NotImplementedError("h3b int8_linear: input_act / residual variants are not covered")
+    if input_act not in (None, "none", "swiglu") or residual is not None:
+        raise NotImplementedError("h3b int8_linear: this input_act / residual variant is not covered")
+    if input_act == "swiglu" and (not convrot or input_act_weight is not None or input_act_eps):
+        raise NotImplementedError("h3b int8_linear: SwiGLU is covered with ConvRot and no activation weight")
     if convrot and convrot_groupsize not in (64, 256):
         raise NotImplementedError(f"h3b int8_linear: ConvRot group {convrot_groupsize} (64 or 256 covered)")
     if (out_dtype or x.dtype) != torch.bfloat16 or x.dtype != torch.bfloat16:
@@ -170,4 +199,5 @@ def int8_linear(x, weight, weight_scale, bias=None, out_dtype=None, convrot=Fals
     ws = weight_scale.reshape(-1).to(torch.float32)
     if ws.numel() != n:
         ws = ws.expand(n).contiguous()
-    return linear(x, weight.contiguous(), ws, bias, convrot_group=convrot_groupsize if convrot else 0)
+    return linear(x, weight.contiguous(), ws, bias, convrot_group=convrot_groupsize if convrot else 0,
+                  swiglu=input_act == "swiglu")

@@ -187,3 +187,36 @@ def test_int8_linear_convrot_vs_oracle():
     np.testing.assert_array_equal(bits(y)[rows], oracle.int8_mm_scaled(q, w.numpy(), s, ws.numpy()))
     with pytest.raises(NotImplementedError):
         h3b.int8_linear(x[:, :K // 2].to(DEV), w[:, :K // 2].to(DEV), ws.to(DEV), convrot=True, convrot_groupsize=128)
+
+
+@pytest.mark.parametrize("M,K,group,scale", [(513, 5120, 256, 1.0), (64, 13824, 256, 4.0), (300, 1024, 64, 0.5)])
+def test_swiglu_quant_convrot_equals_composition(M, K, group, scale):
+    """SwiGLU fused into the ConvRot quantiser == PyTorch's own activation
+    (F.silu(a.float()) * b.float() -> bf16, on the GPU) followed by the ConvRot
+    quantiser, bit for bit; and that composition matches the C restatement."""
+    import torch.nn.functional as F
+    x = randn_bf16((M, 2 * K), seed=M + K + group, scale=scale).to(DEV)
+    act = (F.silu(x[:, :K].float()) * x[:, K:].float()).to(torch.bfloat16)
+    q, s = h3b.swiglu_quant_convrot(x, group)
+    q_ref, s_ref = h3b.quant_rowwise_convrot(act.contiguous(), group)
+    torch.cuda.synchronize()
+    assert torch.equal(s, s_ref), "row scales differ"
+    assert torch.equal(q, q_ref), f"{(q != q_ref).sum().item()} codes differ"
+    rows = np.arange(0, M, max(1, M // 16))
+    qo, so = oracle.quant_rowwise_convrot(bits(act)[rows], group)
+    np.testing.assert_array_equal(q.cpu().numpy()[rows], qo)
+    np.testing.assert_array_equal(s.cpu().numpy().reshape(-1)[rows], so)
+
+
+def test_int8_linear_swiglu_convrot():
+    """int8_linear(input_act="swiglu", convrot=True) on x [M, 2K]: the reference
+    fast path's fc2 call, equal to the oracle GEMM on the fused quantiser's codes."""
+    M, N, K = 512, 1024, 2048
+    x = randn_bf16((M, 2 * K), seed=31).to(DEV)
+    w, ws, _ = _weights(N, K, seed=32)
+    y = h3b.int8_linear(x, w.to(DEV), ws.to(DEV), None, torch.bfloat16, convrot=True, convrot_groupsize=256,
+                        input_act="swiglu")
+    q, s = h3b.swiglu_quant_convrot(x, 256)
+    torch.cuda.synchronize()
+    ref = oracle.int8_mm_scaled(q.cpu().numpy(), w.numpy(), s.cpu().numpy(), ws.numpy())
+    np.testing.assert_array_equal(bits(y), ref)
