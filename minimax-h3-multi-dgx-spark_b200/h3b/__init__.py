@@ -14,11 +14,11 @@ from .fuse import (gate_, gate_norm_mod_, gate_norm_mod_quant_, modulation_table
 from .linear import (gelu_quant, int8_linear, int8_mm_i32, int8_mm_scaled, int8_mm_scaled_a2a, linear,  # noqa: F401
                      quant_rowwise, quant_rowwise_convrot, supported, swiglu_quant_convrot)
 from .sp import (PeerExchange, SPContext, a2a_gather_qkv, a2a_gather_seq_scatter_heads,  # noqa: F401
-                 a2a_scatter_seq_gather_heads, overlap_groups, pack, sp_attention_overlap, startup_probe, unpack)
+                 a2a_scatter_seq_gather_heads, gather_rows, overlap_groups, pack, sp_attention_overlap, startup_probe, unpack)
 
 __all__ = ["H3BError", "status", "clear_status", "norm_mod", "gate_norm_mod_", "gate_", "row_index",
            "norm_mod_quant", "gate_norm_mod_quant_", "gelu_quant",
            "modulation_tables", "quant_rowwise", "quant_rowwise_convrot", "swiglu_quant_convrot", "int8_mm_scaled", "int8_mm_scaled_a2a", "int8_mm_i32", "int8_linear",
            "linear",
            "supported", "SPContext", "PeerExchange", "a2a_gather_seq_scatter_heads", "a2a_scatter_seq_gather_heads",
-           "a2a_gather_qkv", "sp_attention_overlap", "overlap_groups", "pack", "unpack", "startup_probe"]
+           "a2a_gather_qkv", "sp_attention_overlap", "overlap_groups", "gather_rows", "pack", "unpack", "startup_probe"]

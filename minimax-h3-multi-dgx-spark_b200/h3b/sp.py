@@ -7,6 +7,7 @@ Mirrors comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:
   a2a_scatter_seq_gather_heads(t, ctx)      :191-198  [S, (H/P)*D] -> [s_local, H*D]
   sp_attention_overlap(q, k, v, ctx, ...)   :211-261  exchange/attention overlap by head groups
   overlap_groups(hp, world)                 :58,264-273
+  gather_rows(local, counts, ctx, out_dim)  :378-389  padded all-gather of the final rows
 and the known-answer start-up probe of sp_group.py:107-128.
 
 Two exchange back ends, chosen per SPContext (`ctx.exchange`):
@@ -462,6 +463,23 @@ class PeerExchange:
         for b in self._bases:
             check(lib.h3b_ipc_close(ctypes.c_void_p(b)), "h3b_ipc_close")
         self._bases = []
+
+
+def gather_rows(local, counts, ctx, out_dim, device=None):
+    """Every rank's row block, concatenated in rank order on every rank
+    (sp_forward.py:378-389): blocks of counts[r] rows (possibly 0) of out_dim
+    fp32 columns are padded to max(counts) rows for one all-gather, then the
+    padding is dropped.  local: this rank's [counts[rank], out_dim] or None
+    (then `device` names the device of the buffers)."""
+    maxn = max(counts)
+    dev = local.device if local is not None else (device or torch.device("cuda", torch.cuda.current_device()))
+    buf = torch.zeros(maxn, out_dim, dtype=torch.float32, device=dev)
+    if local is not None and local.shape[0]:
+        buf[:local.shape[0]] = local
+    gathered = torch.empty(ctx.world * maxn, out_dim, dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(gathered, buf, group=ctx.group)
+    gathered = gathered.view(ctx.world, maxn, out_dim)
+    return torch.cat([gathered[r, :counts[r]] for r in range(ctx.world) if counts[r] > 0], dim=0)
 
 
 # ---------------------------------------------------------------------------

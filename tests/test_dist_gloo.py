@@ -3,7 +3,7 @@
 Covers the parts of the Ulysses path that are not kernels: SPContext's row
 splits, the exchange calls with their split sizes (h3b.sp._seq_gather /
 _seq_scatter, fed with oracle-packed buffers; whole and per head group), the
-start-up known-answer probe,
+final layer's padded row gather, the start-up known-answer probe,
 and failure detection -- a rank that never reaches the exchange makes the other
 rank's collective fail within the process-group timeout instead of hanging.
 """
@@ -86,6 +86,11 @@ def _worker_exchange(rank, world, port, S, q):
             sp._seq_scatter(recv, torch.from_numpy(part.view(np.float16)).reshape(-1), ctx, w)
             final[:, :, g] = recv.numpy().view(np.uint16).reshape(world, ctx.local, w).transpose(1, 0, 2)
         np.testing.assert_array_equal(final.reshape(ctx.local, -1), sp_layout.a2a_inv(obits, world)[rank])
+        # padded row gather of the final layer (sp_forward.py:378-389), uneven blocks incl. an empty one
+        counts = [3, 0] + [2] * (world - 2)
+        blocks = [torch.arange(n * 5, dtype=torch.float32).view(n, 5) + 100 * r for r, n in enumerate(counts)]
+        got = sp.gather_rows(blocks[rank] if counts[rank] else None, counts, ctx, 5, device=torch.device("cpu"))
+        assert torch.equal(got, torch.cat([b for b in blocks if b.shape[0]], dim=0))
         sp.startup_probe(rank, world, dist.group.WORLD, torch.device("cpu"))
         dist.barrier()
         dist.destroy_process_group()
