@@ -192,26 +192,36 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
     const int64_t row = blockIdx.x;
     const int p = threadIdx.x, lane = p & 31, warp = p >> 5;
     const int r = a.ridx[row];
-    if (r < 0 || r >= a.R) {
-        if (p == 0) report(a.status, H3B_STATUS_BAD_INDEX);
-        return;
-    }
     const int nv = a.D >> 3;
     uint4* xr = reinterpret_cast<uint4*>(a.x + row * (int64_t)a.D);
+    // The row's loads do not depend on its table index: issue them before the
+    // index load completes (the index only selects the modulation rows).
     uint4 v[IT];
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
         const int j = it * kNorm8Threads + p;
         if (j < nv) v[it] = xr[j];
     }
+    uint4 ov[GATE ? IT : 1];
     if constexpr (GATE) {
         const uint4* orow = reinterpret_cast<const uint4*>(a.o + row * (int64_t)a.D);
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+            const int j = it * kNorm8Threads + p;
+            if (j < nv) ov[it] = orow[j];
+        }
+    }
+    if (r < 0 || r >= a.R) {
+        if (p == 0) report(a.status, H3B_STATUS_BAD_INDEX);
+        return;
+    }
+    if constexpr (GATE) {
         const uint4* grow = reinterpret_cast<const uint4*>(a.g + (int64_t)r * a.D);
 #pragma unroll
         for (int it = 0; it < IT; ++it) {
             const int j = it * kNorm8Threads + p;
             if (j < nv) {
-                const uint4 o4 = orow[j], g4 = grow[j];
+                const uint4 o4 = ov[it], g4 = grow[j];
                 v[it] = make_uint4(gate2(v[it].x, o4.x, g4.x), gate2(v[it].y, o4.y, g4.y), gate2(v[it].z, o4.z, g4.z),
                                    gate2(v[it].w, o4.w, g4.w));
                 xr[j] = v[it];
