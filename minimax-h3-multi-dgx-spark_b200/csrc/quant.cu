@@ -28,16 +28,22 @@ namespace h3b {
 
 enum class Act { kNone = 0, kGeluTanh = 1 };
 
-__device__ __forceinline__ float gelu_tanh(float x) {
+// bf16(gelu_tanh(x)) of two elements: PyTorch's GeluCUDAKernelImpl formula in
+// fp32, x^3 as (x*x)*x, inner = kBeta * fma(kKappa, x^3, x), 0.5*x*(1+tanhf(inner)),
+// each operation rounded once, on fp32 pairs (f32x2 instructions round each
+// lane exactly as the scalar ones).
+__device__ __forceinline__ uint32_t gelu2(uint32_t v) {
     constexpr float kBeta = (float)(1.41421356237309504880 * 1.12837916709551257390 * 0.5);
     constexpr float kKappa = (float)0.044715;
-    const float x3 = __fmul_rn(__fmul_rn(x, x), x);
-    const float inner = __fmul_rn(kBeta, __fmaf_rn(kKappa, x3, x));
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
-}
-
-__device__ __forceinline__ uint32_t gelu2(uint32_t v) {
-    return pack_bf16x2(gelu_tanh(bf16_lo(v)), gelu_tanh(bf16_hi(v)));
+    const uint64_t x = f2(bf16_lo(v), bf16_hi(v));
+    const uint64_t x3 = mul2(mul2(x, x), x);
+    const uint64_t inner = mul2(f2(kBeta, kBeta), fma2(f2(kKappa, kKappa), x3, x));
+    float i0, i1;
+    f2_split(inner, i0, i1);
+    const uint64_t t1 = add2(f2(1.0f, 1.0f), f2(tanhf(i0), tanhf(i1)));
+    float y0, y1;
+    f2_split(mul2(mul2(f2(0.5f, 0.5f), x), t1), y0, y1);
+    return pack_bf16x2(y0, y1);
 }
 
 constexpr int kMaxGatherRanks = 8;
@@ -118,11 +124,6 @@ __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __res
 // 1/sqrt(G); two elements per f32x2 instruction.  Every lane runs every
 // shuffle (lanes past the row's end carry zeros), so the full-warp shuffles
 // never see an exited lane.
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
 __device__ __forceinline__ uint64_t shfl_xor2(uint64_t v, int m) {
     return __shfl_xor_sync(0xffffffffu, (unsigned long long)v, m);
 }

@@ -48,6 +48,11 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
 
 // 8 values -> 8 int8 codes packed into two 32-bit words (s == 0 gives zeros).
 // Fast path for all 8: t = x * r, m = t + magic (code in m's low byte),

@@ -188,7 +188,7 @@ FUSED_EXCHANGE = os.environ.get("H3B_FUSED_EXCHANGE", "1") != "0"
 # (H3B_FUSED_NORM_QUANT, H3B_FUSED_GELU_QUANT = 0 / 1); the defaults are the
 # faster form as measured in the block.
 FUSED_NORM_QUANT = os.environ.get("H3B_FUSED_NORM_QUANT", "0") == "1"
-FUSED_GELU_QUANT = os.environ.get("H3B_FUSED_GELU_QUANT", "0") == "1"
+FUSED_GELU_QUANT = os.environ.get("H3B_FUSED_GELU_QUANT", "1") == "1"
 
 
 def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, overlap_groups=None):
