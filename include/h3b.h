@@ -173,6 +173,14 @@ H3B_API int h3b_int8_linear_noalloc(const void *x, int64_t M, int64_t K, const i
 H3B_API int h3b_norm_mod(const void *x, const void *w, float eps, const int32_t *ridx, const void *s1, const void *sh,
                  void *h, int64_t S, int64_t D, int64_t R, void *stream);
 
+/* Plain RMSNorm with a weight, no modulation: h = rbf16(w * (rstd * x)),
+ * rstd = rsqrt(sum(x^2) / D + eps), the same reduction order and rounding as
+ * h3b_norm_mod's first step (PyTorch's F.rms_norm(x, (D,), w, eps)).  x, h bf16
+ * [S, D], w bf16 [D], D % 8 == 0, 16-byte aligned.  Covers the per-head q/k norm
+ * of sp_attention when it has no RoPE (x = [S*H, head_dim]),
+ * comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:296-298. */
+H3B_API int h3b_rms_norm(const void *x, const void *w, float eps, void *h, int64_t S, int64_t D, void *stream);
+
 /* x <- bf16(x + o * g[r]) in place, then h = norm_mod(x).
  * Replaces gate_norm_mod_, h3_fuse_kernels.py:181-185 (kernel :117-155). */
 H3B_API int h3b_gate_norm_mod_(void *x, const void *o, const void *g, const void *w, float eps, const int32_t *ridx,

@@ -176,6 +176,13 @@ __device__ __forceinline__ uint32_t norm2(uint32_t xp, float rstd, uint32_t wp, 
     return pack_bf16x2(__fadd_rn(bf16_lo(z), bf16_lo(hp)), __fadd_rn(bf16_hi(z), bf16_hi(hp)));
 }
 
+// Plain RMSNorm with weight (no modulation): rbf16(w * (rstd * x)), the first
+// rounding point of norm2 -- F.rms_norm's output.
+__device__ __forceinline__ uint32_t rms2(uint32_t xp, float rstd, uint32_t wp) {
+    return pack_bf16x2(__fmul_rn(bf16_lo(wp), __fmul_rn(rstd, bf16_lo(xp))),
+                       __fmul_rn(bf16_hi(wp), __fmul_rn(rstd, bf16_hi(xp))));
+}
+
 __device__ __forceinline__ uint32_t gate2(uint32_t xp, uint32_t op, uint32_t gp) {
     return pack_bf16x2(gate1(bf16_lo(xp), bf16_lo(op), bf16_lo(gp)), gate1(bf16_hi(xp), bf16_hi(op), bf16_hi(gp)));
 }
@@ -191,7 +198,7 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
                                                               float* __restrict__ xs) {
     const int64_t row = blockIdx.x;
     const int p = threadIdx.x, lane = p & 31, warp = p >> 5;
-    const int r = a.ridx[row];
+    const int r = a.ridx ? a.ridx[row] : 0;  // no table index: plain RMSNorm (s1 == sh == NULL)
     const int nv = a.D >> 3;
     uint4* xr = reinterpret_cast<uint4*>(a.x + row * (int64_t)a.D);
     // The row's loads do not depend on its table index: issue them before the
@@ -250,6 +257,7 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
     const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.D), a.eps));
 
     const uint4* wv = reinterpret_cast<const uint4*>(a.w);
+    const bool modulate = a.s1 != nullptr;
     const uint4* s1r = reinterpret_cast<const uint4*>(a.s1 + (int64_t)r * a.D);
     const uint4* shr = reinterpret_cast<const uint4*>(a.sh + (int64_t)r * a.D);
     uint4* hr = reinterpret_cast<uint4*>(a.h + row * (int64_t)a.D);
@@ -258,9 +266,16 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
     for (int it = 0; it < IT; ++it) {
         const int j = it * kNorm8Threads + p;
         if (j < nv) {
-            const uint4 w4 = wv[j], s4 = s1r[j], h4 = shr[j];
-            const uint4 y = make_uint4(norm2(v[it].x, rstd, w4.x, s4.x, h4.x), norm2(v[it].y, rstd, w4.y, s4.y, h4.y),
-                                       norm2(v[it].z, rstd, w4.z, s4.z, h4.z), norm2(v[it].w, rstd, w4.w, s4.w, h4.w));
+            const uint4 w4 = wv[j];
+            uint4 y;
+            if (modulate) {
+                const uint4 s4 = s1r[j], h4 = shr[j];
+                y = make_uint4(norm2(v[it].x, rstd, w4.x, s4.x, h4.x), norm2(v[it].y, rstd, w4.y, s4.y, h4.y),
+                               norm2(v[it].z, rstd, w4.z, s4.z, h4.z), norm2(v[it].w, rstd, w4.w, s4.w, h4.w));
+            } else {
+                y = make_uint4(rms2(v[it].x, rstd, w4.x), rms2(v[it].y, rstd, w4.y), rms2(v[it].z, rstd, w4.z),
+                               rms2(v[it].w, rstd, w4.w));
+            }
             if constexpr (Q8) {
                 v[it] = y;
                 m = absmax_bits8(y, m);
@@ -429,4 +444,18 @@ extern "C" int h3b_gate_norm_mod_quant_(void* x, const void* o, const void* g, c
                static_cast<const uint16_t*>(sh), nullptr, eps, (int)D, (int)R, ds.word};
     H3B_REQUIRE(norm8_ok(a), "h3b_gate_norm_mod_quant_: needs D %% 8 == 0 and 16-byte aligned tensors");
     return launch_norm8<true, true>(a, S, xq, xs, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_rms_norm(const void* x, const void* w, float eps, void* h, int64_t S, int64_t D, void* stream) {
+    H3B_REQUIRE(x && w && h, "h3b_rms_norm: NULL pointer");
+    H3B_REQUIRE(S >= 0 && S < (1ll << 31), "h3b_rms_norm: bad S=%lld", (long long)S);
+    H3B_REQUIRE(D > 0 && D % 8 == 0 && D <= 16384, "h3b_rms_norm: D=%lld must be a positive multiple of 8 <= 16384",
+                (long long)D);
+    if (S == 0) return H3B_OK;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    NormArgs a{const_cast<uint16_t*>(static_cast<const uint16_t*>(x)), nullptr, nullptr, static_cast<const uint16_t*>(w),
+               nullptr, nullptr, nullptr, static_cast<uint16_t*>(h), eps, (int)D, 1, ds.word};
+    H3B_REQUIRE(norm8_ok(a), "h3b_rms_norm: x, w and h must be 16-byte aligned");
+    return launch_norm8<false, false>(a, S, nullptr, nullptr, static_cast<cudaStream_t>(stream));
 }

@@ -33,6 +33,7 @@ SIGNATURES = [
     ("h3b_int8_linear", _I32, [_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _P, _P]),
     ("h3b_int8_linear_noalloc", _I32, [_P, _I64, _I64, _P, _P, _P, _I64, _P, _P]),
     ("h3b_norm_mod", _I32, [_P, _P, _F32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    ("h3b_rms_norm", _I32, [_P, _P, ctypes.c_float, _P, _I64, _I64, _P]),
     ("h3b_gate_norm_mod_", _I32, [_P, _P, _P, _P, _F32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_gate_", _I32, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_norm_mod_quant", _I32, [_P, _P, _F32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),

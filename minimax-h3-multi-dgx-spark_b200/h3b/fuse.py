@@ -43,6 +43,21 @@ def norm_mod(x, w, eps, ridx, s1, sh):
     return h
 
 
+def rms_norm(x, w, eps):
+    """F.rms_norm(x, (D,), w, eps) over the last dimension, bit for bit (bf16 in and out):
+    the per-head q/k norm of sp_attention without RoPE (sp_forward.py:296-298)."""
+    require_cuda(x, w)
+    D = x.shape[-1]
+    if x.dtype != BF16 or w.dtype != BF16 or w.numel() != D or not x.is_contiguous():
+        raise ValueError("rms_norm: x must be contiguous bf16 [..., D] and w bf16 [D]")
+    x2 = x.view(-1, D)
+    h = torch.empty_like(x)
+    with span("rms_norm", 4 * x.numel()):
+        check(lib.h3b_rms_norm(ptr(x2), ptr(w.contiguous()), float(eps), ptr(h), x2.shape[0], D, stream_of(x)),
+              "h3b_rms_norm")
+    return h
+
+
 def gate_norm_mod_(x, o, g, w, eps, ridx, s1, sh):
     """x <- bf16(x + o * g[r]) in place; returns h = norm_mod(x)."""
     S, D, R = _check(x, w, ridx, s1, sh)

@@ -176,3 +176,15 @@ def test_norm_fallback_kernel_d_mod8_4(S, D):
     h2 = h3b.gate_norm_mod_(xd, od, gd, wd, 1e-6, rd, s1d, shd)
     assert torch.equal(xd.view(torch.int16), x_ref.view(torch.int16))
     assert torch.equal(h2.view(torch.int16), _eager_norm_mod(x_ref, wd, 1e-6, rd, s1d, shd).view(torch.int16))
+
+
+@pytest.mark.parametrize("shape", [(4128, 40, 128), (777, 5, 128), (2048, 5120), (33, 1024)])
+def test_rms_norm_equals_torch(shape):
+    """Plain RMSNorm (the per-head q/k norm, head_dim 128, and full rows) against
+    PyTorch's F.rms_norm on the GPU, bit for bit."""
+    x = adversarial_rows(int(np.prod(shape[:-1])), shape[-1], seed=sum(shape)).view(*shape).to(DEV)
+    w = (1 + 0.02 * torch.randn(shape[-1], generator=gen(7))).to(torch.bfloat16).to(DEV)
+    h = h3b.rms_norm(x, w, 1e-6)
+    ref = F.rms_norm(x, (shape[-1],), w, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(h.view(torch.int16), ref.view(torch.int16)), f"{(h != ref).sum().item()} elements differ"
