@@ -139,6 +139,20 @@ H3B_API int h3b_int8_mm_scaled_a2a(const int8_t *xq, const int8_t *w, const floa
                                    int64_t row_start, int64_t seg_cols, int64_t head_dim, int64_t heads_per_rank,
                                    int world, void *stream);
 
+/* h3b_int8_mm_scaled_a2a with the attention's per-head q / k RMSNorm in the
+ * epilogue: every 128-column head of the first norm_segs segments (q, then k)
+ * of each row becomes rbf16(w_t * (rstd * y)), rstd = rsqrt(sum(y^2)/128 + eps),
+ * y the bf16 projection output and w_t = norm_w + t * 128 (bf16 [norm_segs, 128]),
+ * with the reduction order of h3b_rms_norm / F.rms_norm, before it is stored
+ * into the owning rank's receive buffer.  head_dim == 128.  Replaces the qkv
+ * projection, attn.q_norm / attn.k_norm and the forward exchange of
+ * sp_attention, sp_forward.py:280-284,296-298,308-311 (the no-RoPE branch). */
+H3B_API int h3b_int8_mm_scaled_a2a_qknorm(const int8_t *xq, const int8_t *w, const float *xs, const float *ws,
+                                          const void *bias, int64_t M, int64_t N, int64_t K, void *const *dst,
+                                          int64_t row_start, int64_t seg_cols, int64_t head_dim,
+                                          int64_t heads_per_rank, int world, const void *norm_w, int64_t norm_segs,
+                                          float norm_eps, void *stream);
+
 /* Patched Linear forward: quantise x (h3b_quant_rowwise) into the caller's
  * scratch xq [M,K] / xs [M], then h3b_int8_mm_scaled into out [M,N].
  * Replaces the patched comfy_kitchen.backends.cuda.int8_linear,

@@ -65,6 +65,12 @@ struct Scatter {
     uint16_t* dst[kMaxScatterSegs * kMaxScatterWorld];
     int64_t row_start;
     int seg, head_dim, hp, world;
+    // Optional per-head RMSNorm of the first norm_segs segments (the q and k
+    // norms of the attention): each 128-column head of those segments becomes
+    // rbf16(w_t * (rstd * y)), w_t = norm_w + t * 128, before it is stored.
+    const uint16_t* norm_w;
+    int norm_segs;
+    float norm_eps;
 };
 
 struct Args {
@@ -243,6 +249,8 @@ __device__ __forceinline__ void store_chunk(const Args& args, const uint32_t (&r
 // 128-byte lines -- full NVLink writes when the destination is a peer.
 // Requires seg % head_dim == 0 and head_dim % 64 == 0 (a unit never straddles
 // a head, so its destination is warp-uniform).
+__device__ __forceinline__ void store_stage(const Args& args, const uint4* stage, int row0, int col0, int lane);
+
 __device__ __forceinline__ void scatter_unit(const Args& args, uint4* stage, uint32_t t_col, int row0, int col0,
                                             float xs, int lane) {
     uint32_t r[32];
@@ -254,6 +262,12 @@ __device__ __forceinline__ void scatter_unit(const Args& args, uint4* stage, uin
     for (int g = 0; g < 4; ++g)
         stage[lane * 8 + ((g + 4) ^ (lane & 7))] = dequant8(args, r + 8 * g, col0 + 32 + 8 * g, xs);
     __syncwarp();
+    store_stage(args, stage, row0, col0, lane);
+}
+
+// The staged 32 rows x 64 columns (columns col0 ..) to the owning rank's
+// receive buffer, 8 lanes per row.
+__device__ __forceinline__ void store_stage(const Args& args, const uint4* stage, int row0, int col0, int lane) {
     const Scatter& sc = args.sc;
     const int t = col0 / sc.seg, within = col0 - t * sc.seg;
     const int h = within / sc.head_dim, j = h / sc.hp;
@@ -267,6 +281,70 @@ __device__ __forceinline__ void scatter_unit(const Args& args, uint4* stage, uin
         if (grow < args.M) *reinterpret_cast<uint4*>(dbase + (sc.row_start + grow) * dld + cc * 8) = v;
     }
     __syncwarp();
+}
+
+// Scatter epilogue of one 128-column head with its RMSNorm (q / k norm): the
+// lane's row of the head is dequantised to bf16 (the projection's output),
+// its sum of squares is formed in the order PyTorch's F.rms_norm uses for a
+// 128-wide row (32 partial sums of 4 consecutive elements, each an FMA chain
+// from 0, then the shuffle-down tree 16, 8, 4, 2, 1 over the partials; the
+// other warps of that reduction contribute exact zeros), rstd =
+// rsqrtf(sum / 128 + eps), and each element becomes rbf16(w * (rstd * y)).
+// The normalised head is stored as two staged 64-column halves.
+__device__ __forceinline__ void scatter_head_norm(const Args& args, uint4* stage, uint32_t t_col, int row0, int col0,
+                                                 float xs, int lane, const uint16_t* __restrict__ w) {
+    uint32_t hw[64];  // the head's 128 bf16 values, packed in pairs
+    float part[16];   // partial sums after the tree's first level (16)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_col + 32u * c, r);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint4 v = dequant8(args, r + 8 * g, col0 + 32 * c + 8 * g, xs);
+            hw[16 * c + 4 * g + 0] = v.x;
+            hw[16 * c + 4 * g + 1] = v.y;
+            hw[16 * c + 4 * g + 2] = v.z;
+            hw[16 * c + 4 * g + 3] = v.w;
+        }
+        // partials of virtual threads 8c .. 8c+7 (elements 4vt .. 4vt+3 = words 2vt, 2vt+1)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int vt = 8 * c + k;
+            float acc = 0.0f;
+            acc = __fmaf_rn(bf16_lo(hw[2 * vt]), bf16_lo(hw[2 * vt]), acc);
+            acc = __fmaf_rn(bf16_hi(hw[2 * vt]), bf16_hi(hw[2 * vt]), acc);
+            acc = __fmaf_rn(bf16_lo(hw[2 * vt + 1]), bf16_lo(hw[2 * vt + 1]), acc);
+            acc = __fmaf_rn(bf16_hi(hw[2 * vt + 1]), bf16_hi(hw[2 * vt + 1]), acc);
+            if (c < 2) part[vt] = acc;                          // vt < 16
+            else part[vt - 16] = __fadd_rn(part[vt - 16], acc);  // tree level 16
+        }
+    }
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1)
+#pragma unroll
+        for (int vt = 0; vt < off; ++vt) part[vt] = __fadd_rn(part[vt], part[vt + off]);
+    const float tot = __fadd_rn(__fadd_rn(part[0], 0.0f), __fadd_rn(0.0f, 0.0f));
+    const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(tot, 128.0f), args.sc.norm_eps));
+    const uint4* wv = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const uint4 w4 = wv[8 * half + g];
+            const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t x = hw[32 * half + 4 * g + e];
+                o[e] = pack_bf16x2(__fmul_rn(bf16_lo(ww[e]), __fmul_rn(rstd, bf16_lo(x))),
+                                   __fmul_rn(bf16_hi(ww[e]), __fmul_rn(rstd, bf16_hi(x))));
+            }
+            stage[lane * 8 + (g ^ (lane & 7))] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        __syncwarp();
+        store_stage(args, stage, row0, col0 + 64 * half, lane);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -680,10 +758,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // 64-column units (TILE_N % 64 == 0 and N % 64 == 0 for this variant)
                 uint4* stage = reinterpret_cast<uint4*>(base + STAGES * STAGE_BYTES + 256) + q * (32 * 8);
 #pragma unroll 1
-                for (int c = 0; c < TILE_N / 64; ++c) {
+                for (int c = 0; c < TILE_N / 64;) {
                     const int col0 = nb * TILE_N + c * 64;
                     if (col0 >= N) break;  // warp-uniform
-                    scatter_unit(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane);
+                    const int t = col0 / args.sc.seg;
+                    if (t < args.sc.norm_segs) {
+                        // a whole 128-column head (tile_n % 128 == 0 for this case)
+                        scatter_head_norm(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane,
+                                          args.sc.norm_w + t * 128);
+                        c += 2;
+                    } else {
+                        scatter_unit(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane);
+                        ++c;
+                    }
                 }
             } else {
 #pragma unroll 1
@@ -759,7 +846,7 @@ static int num_sms() {
 // (rounds of pair tiles over the resident pairs) x (256 + t); ties go to the
 // wider tile.  Wave quantisation picks 224 for config 0's 4096 x 5120; large M
 // keeps 256.
-static int pick_tile_n(int M, int N, int64_t pairs, bool mult64 = false) {
+static int pick_tile_n(int M, int N, int64_t pairs, int multiple = 32) {
     // H3B_GEMM_TILE_N (a multiple of 32 in 32..256) pins the width, for tuning sweeps
     static int forced = -1;
     if (forced < 0) {
@@ -767,13 +854,13 @@ static int pick_tile_n(int M, int N, int64_t pairs, bool mult64 = false) {
         const int v = e ? atoi(e) : 0;
         forced = (v >= 32 && v <= 256 && v % 32 == 0) ? v : 0;
     }
-    if (forced && (!mult64 || forced % 64 == 0)) return forced;
+    if (forced && forced % multiple == 0) return forced;
     static const int cands[] = {256, 224, 192, 160, 128};
     const int64_t m_tiles = (M + pair::TILE_M - 1) / pair::TILE_M;
     int best = 256;
     int64_t best_cost = -1;
     for (int t : cands) {
-        if (mult64 && t % 64) continue;
+        if (t % multiple) continue;
         const int64_t tiles = m_tiles * ((N + t - 1) / t);
         const int64_t rounds = (tiles + pairs - 1) / pairs;
         const int64_t cost = rounds * (256 + t);
@@ -854,7 +941,7 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
         H3B_CUDA_TRY(cudaFuncSetAttribute(pair::gemm_i8_pair_kernel<OUT_I32, SCATTER>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         const int64_t pairs_max = max_pairs<OUT_I32, SCATTER>();
-        a.tile_n = pick_tile_n(a.M, a.N, pairs_max, SCATTER);
+        a.tile_n = pick_tile_n(a.M, a.N, pairs_max, !SCATTER ? 32 : (a.sc.norm_segs > 0 ? 128 : 64));
         if (int rc = make_map(&tmB, w, a.N, a.K, (uint32_t)(a.tile_n / 2))) return rc;
         const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + a.tile_n - 1) / a.tile_n);
         const int pairs = (int)(tiles < pairs_max ? tiles : pairs_max);
@@ -893,10 +980,37 @@ extern "C" int h3b_int8_mm_i32(const int8_t* xq, const int8_t* w, int32_t* acc, 
     return gemm::launch<true>(xq, w, a, static_cast<cudaStream_t>(stream));
 }
 
+static int mm_scaled_a2a(const int8_t* xq, const int8_t* w, const float* xs, const float* ws, const void* bias,
+                         int64_t M, int64_t N, int64_t K, void* const* dst, int64_t row_start, int64_t seg_cols,
+                         int64_t head_dim, int64_t heads_per_rank, int world, const void* norm_w, int64_t norm_segs,
+                         float norm_eps, void* stream);
+
 extern "C" int h3b_int8_mm_scaled_a2a(const int8_t* xq, const int8_t* w, const float* xs, const float* ws,
                                       const void* bias, int64_t M, int64_t N, int64_t K, void* const* dst,
                                       int64_t row_start, int64_t seg_cols, int64_t head_dim, int64_t heads_per_rank,
                                       int world, void* stream) {
+    return mm_scaled_a2a(xq, w, xs, ws, bias, M, N, K, dst, row_start, seg_cols, head_dim, heads_per_rank, world,
+                         nullptr, 0, 0.0f, stream);
+}
+
+extern "C" int h3b_int8_mm_scaled_a2a_qknorm(const int8_t* xq, const int8_t* w, const float* xs, const float* ws,
+                                             const void* bias, int64_t M, int64_t N, int64_t K, void* const* dst,
+                                             int64_t row_start, int64_t seg_cols, int64_t head_dim,
+                                             int64_t heads_per_rank, int world, const void* norm_w, int64_t norm_segs,
+                                             float norm_eps, void* stream) {
+    H3B_REQUIRE(norm_w && norm_segs >= 1 && norm_segs <= N / (seg_cols > 0 ? seg_cols : 1) && head_dim == 128 &&
+                    aligned(norm_w, 16),
+                "h3b_int8_mm_scaled_a2a_qknorm: norm_w (16-byte aligned, [norm_segs, 128]) and 1 <= norm_segs <= "
+                "segments with head_dim 128 required (norm_segs=%lld head_dim=%lld)",
+                (long long)norm_segs, (long long)head_dim);
+    return mm_scaled_a2a(xq, w, xs, ws, bias, M, N, K, dst, row_start, seg_cols, head_dim, heads_per_rank, world,
+                         norm_w, norm_segs, norm_eps, stream);
+}
+
+static int mm_scaled_a2a(const int8_t* xq, const int8_t* w, const float* xs, const float* ws, const void* bias,
+                         int64_t M, int64_t N, int64_t K, void* const* dst, int64_t row_start, int64_t seg_cols,
+                         int64_t head_dim, int64_t heads_per_rank, int world, const void* norm_w, int64_t norm_segs,
+                         float norm_eps, void* stream) {
     H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_scaled_a2a: shape out of range");
     H3B_REQUIRE(dst && world >= 1 && world <= gemm::kMaxScatterWorld && row_start >= 0,
                 "h3b_int8_mm_scaled_a2a: bad dst / world=%d / row_start", world);
@@ -917,6 +1031,9 @@ extern "C" int h3b_int8_mm_scaled_a2a(const int8_t* xq, const int8_t* w, const f
     a.sc.head_dim = (int)head_dim;
     a.sc.hp = (int)heads_per_rank;
     a.sc.world = world;
+    a.sc.norm_w = static_cast<const uint16_t*>(norm_w);
+    a.sc.norm_segs = (int)norm_segs;
+    a.sc.norm_eps = norm_eps;
     return gemm::launch<false, true>(xq, w, a, static_cast<cudaStream_t>(stream));
 }
 

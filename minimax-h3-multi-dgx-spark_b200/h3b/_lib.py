@@ -30,6 +30,8 @@ SIGNATURES = [
     ("h3b_int8_mm_scaled", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_int8_mm_i32", _I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_int8_mm_scaled_a2a", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _PP, _I64, _I64, _I64, _I64, _I32, _P]),
+    ("h3b_int8_mm_scaled_a2a_qknorm", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _PP, _I64, _I64, _I64, _I64, _I32,
+                                             _P, _I64, ctypes.c_float, _P]),
     ("h3b_int8_linear", _I32, [_P, _I64, _I64, _P, _P, _P, _I64, _P, _P, _P, _P]),
     ("h3b_int8_linear_noalloc", _I32, [_P, _I64, _I64, _P, _P, _P, _I64, _P, _P]),
     ("h3b_norm_mod", _I32, [_P, _P, _F32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),

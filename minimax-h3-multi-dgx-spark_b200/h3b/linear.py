@@ -121,12 +121,15 @@ def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
     return out
 
 
-def int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst_ptrs, row_start, seg, head_dim, heads_per_rank, world):
+def int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst_ptrs, row_start, seg, head_dim, heads_per_rank, world, norm_w=None,
+                       norm_eps=1e-6):
     """int8_mm_scaled whose epilogue stores column n of the [M,N] product into
     the receive buffer of the rank owning its head (h3b_int8_mm_scaled_a2a):
     dst_ptrs = device addresses [segment * world + rank] of bf16 buffers with
     rows of heads_per_rank*head_dim elements and at least row_start + M rows
-    (the caller guarantees their size).  Returns nothing; the receivers see the
+    (the caller guarantees their size).  norm_w (bf16 [n, 128]): the first n
+    segments (q, k) get a per-head RMSNorm with these weights in the epilogue
+    (h3b_int8_mm_scaled_a2a_qknorm).  Returns nothing; the receivers see the
     rows after a peer barrier."""
     M, N, K = _gemm_checks(xq, w)
     xs = xs.reshape(-1)
@@ -140,9 +143,20 @@ def int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst_ptrs, row_start, seg, head_dim, 
     if len(dst_ptrs) != (N // seg) * world:
         raise ValueError("int8_mm_scaled_a2a: one destination per segment and rank")
     arr, keep = ptr_array(dst_ptrs)
-    with span("gemm_a2a", 2 * M * N * K):
-        check(lib.h3b_int8_mm_scaled_a2a(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), M, N, K, arr, row_start, seg,
-                                         head_dim, heads_per_rank, world, stream_of(xq)), "h3b_int8_mm_scaled_a2a")
+    if norm_w is not None:
+        if norm_w.dtype != torch.bfloat16 or norm_w.dim() != 2 or norm_w.shape[1] != head_dim:
+            raise ValueError("int8_mm_scaled_a2a: norm_w must be bf16 [segments, head_dim]")
+        norm_w = norm_w.contiguous()
+        with span("gemm_a2a", 2 * M * N * K):
+            check(lib.h3b_int8_mm_scaled_a2a_qknorm(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), M, N, K, arr,
+                                                    row_start, seg, head_dim, heads_per_rank, world, ptr(norm_w),
+                                                    norm_w.shape[0], float(norm_eps), stream_of(xq)),
+                  "h3b_int8_mm_scaled_a2a_qknorm")
+    else:
+        with span("gemm_a2a", 2 * M * N * K):
+            check(lib.h3b_int8_mm_scaled_a2a(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), M, N, K, arr, row_start,
+                                             seg, head_dim, heads_per_rank, world, stream_of(xq)),
+                  "h3b_int8_mm_scaled_a2a")
     del keep
 
 

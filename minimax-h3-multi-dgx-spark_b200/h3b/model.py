@@ -72,6 +72,7 @@ class BlockParams:
     cq: Linear8 = None
     ckv: Linear8 = None
     cout: Linear8 = None
+    qkn: torch.Tensor = None  # bf16 [2, head_dim]: q and k RMSNorm weights (qk_norm only)
     tables: tuple = field(default=None, repr=False)
 
 
@@ -84,6 +85,7 @@ class DiTConfig:
     eps: float = 1e-6
     n_blocks: int = 1
     text_len: int = 0  # > 0 enables the cross-attention branch
+    qk_norm: bool = False  # per-head RMSNorm of q and k (attn.q_norm / k_norm), no RoPE
 
 
 def make_params(cfg, block_index, seed, device, R=1):
@@ -103,6 +105,8 @@ def make_params(cfg, block_index, seed, device, R=1):
         p.cq = Linear8.random(D, D, g, device)
         p.ckv = Linear8.random(2 * D, D, g, device)
         p.cout = Linear8.random(D, D, g, device)
+    if cfg.qk_norm:
+        p.qkn = (1 + 0.02 * torch.randn(2, cfg.head_dim, generator=g, device=device)).to(BF16)
     p.tables = fuse.modulation_tables(*(p.e[:, i] for i in range(6)))
     return p
 
@@ -144,14 +148,19 @@ def self_attention(cfg, p, hq, ctx, overlap_groups=None):
     n = (sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups) if sharded else 0
     overlap = n > 1 and hp % n == 0
     if sharded and not overlap and ctx.exchange == "p2p" and FUSED_EXCHANGE:
-        # the qkv GEMM's epilogue stores q, k, v straight into the owners' buffers;
-        # the out projection's quantiser gathers its rows from every rank's output
-        q, k, v = ctx.peer.gemm_fwd(hq[0], hq[1], p.qkv.w, p.qkv.ws, p.qkv.b, ctx)
+        # the qkv GEMM's epilogue (with the q/k norms when the block has them)
+        # stores q, k, v straight into the owners' buffers; the out projection's
+        # quantiser gathers its rows from every rank's output
+        q, k, v = ctx.peer.gemm_fwd(hq[0], hq[1], p.qkv.w, p.qkv.ws, p.qkv.b, ctx,
+                                    norm_w=p.qkn if cfg.qk_norm else None, norm_eps=cfg.eps)
         return _lin_q(ctx.peer.inv_quant(sdpa(q, k, v), ctx), p.out)
     qkv = _lin_q(hq, p.qkv)  # [s, 3D]
     q = qkv[:, :D].view(s, H, Dh)
     k = qkv[:, D:2 * D].view(s, H, Dh)
     v = qkv[:, 2 * D:].view(s, H, Dh)
+    if cfg.qk_norm:
+        q = fuse.rms_norm(q.contiguous(), p.qkn[0], cfg.eps)
+        k = fuse.rms_norm(k.contiguous(), p.qkn[1], cfg.eps)
     if not sharded:
         return _lin(sdpa_heads(q, k, v), p.out)
     if overlap:

@@ -343,12 +343,13 @@ class PeerExchange:
                                       g * w * es, self.world, stream_of(srcs[0])), "h3b_a2a_fwd_p2p")
         del k1, k2
 
-    def gemm_fwd(self, xq, xs, w, ws, bias, ctx):
+    def gemm_fwd(self, xq, xs, w, ws, bias, ctx, norm_w=None, norm_eps=1e-6):
         """A projection fused with the forward exchange (h3b_int8_mm_scaled_a2a):
         the [s_local, n*H*Dh] product of the quantised rows (xq, xs) and w
         (n = 1..3 segments, e.g. the fused q|k|v projection) is stored by the
-        GEMM's epilogue straight into every rank's receive buffers.  Returns the
-        n views [S, H/P, Dh] of this rank's receive buffers."""
+        GEMM's epilogue straight into every rank's receive buffers; with norm_w
+        (bf16 [2, 128]) q and k get their per-head RMSNorm in the same epilogue.
+        Returns the n views [S, H/P, Dh] of this rank's receive buffers."""
         from .linear import int8_mm_scaled_a2a
         D = self.heads * self.head_dim
         nseg = w.shape[0] // D
@@ -359,7 +360,7 @@ class PeerExchange:
         dst = [self.peer_recv[t][j] for t in range(nseg) for j in range(self.world)]
         self.barrier(xq)
         int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst, ctx.start, D, self.head_dim, self.heads // self.world,
-                           self.world)
+                           self.world, norm_w=norm_w, norm_eps=norm_eps)
         self.barrier(xq)
         return self.recv_views(nseg, ctx)
 

@@ -100,6 +100,9 @@ def block_forward(cfg, p, x, ridx, ctx=None, text=None):
     h = norm_mod(x, p.n1w, cfg.eps, ridx, s1a, sha)
     qkv = linear(h, p.qkv.w, p.qkv.ws, p.qkv.b)
     q, k, v = qkv[:, :D].view(s, H, Dh), qkv[:, D:2 * D].view(s, H, Dh), qkv[:, 2 * D:].view(s, H, Dh)
+    if getattr(cfg, "qk_norm", False):  # attn.q_norm / k_norm without RoPE, sp_forward.py:296-298
+        q = F.rms_norm(q, (Dh,), p.qkn[0], cfg.eps)
+        k = F.rms_norm(k, (Dh,), p.qkn[1], cfg.eps)
     if ctx is not None and ctx.world > 1:
         q, k, v = (a2a_gather_seq_scatter_heads(t, ctx) for t in (q, k, v))
         o = a2a_scatter_seq_gather_heads(sdpa_heads(q, k, v), ctx)

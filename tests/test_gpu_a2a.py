@@ -210,6 +210,46 @@ def test_inv_quant_emulated(world, S):
         assert torch.equal(xs.reshape(-1), s_ref.reshape(-1)), f"rank {r}: scales differ"
 
 
+@pytest.mark.parametrize("world,S,heads,K", [(2, 1001, 40, 256), (8, 2000, 40, 384), (1, 300, 8, 128),
+                                             (4, 4130, 40, 5120)])
+def test_gemm_a2a_qknorm_emulated(world, S, heads, K):
+    """The qkv GEMM with the per-head q/k RMSNorm and the exchange in its
+    epilogue: each rank's receive buffers equal the forward exchange of
+    F.rms_norm applied (on the GPU, per 128-wide head) to the unfused GEMM's q and
+    k; v passes through unnormalised."""
+    import torch.nn.functional as F
+    from gpu_util import adversarial_rows, gen
+    splits = sp_layout.splits(S, world)
+    starts = sp_layout.starts(S, world)
+    hp = heads // world
+    D = heads * DH
+    g = gen(world * 77 + S + K)
+    w = torch.randint(-127, 128, (3 * D, K), generator=g, dtype=torch.int8).to(DEV)
+    ws = (torch.rand(3 * D, generator=g) * 9e-3 + 1e-3).to(DEV)
+    ws[:D // 2] *= 40  # wide per-head magnitudes for the norm
+    bias = (torch.randn(3 * D, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    nw = (1 + 0.05 * torch.randn(2, DH, generator=g)).to(torch.bfloat16).to(DEV)
+    xq = [torch.randint(-127, 128, (n, K), generator=g, dtype=torch.int8).to(DEV) for n in splits]
+    xs = [(torch.logspace(-3, 0, n)[:, None] * 0.05).float().to(DEV) for n in splits]
+    recv = [[torch.full((S, hp * DH), -7.0, dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+            for _ in range(3)]
+    dst = [recv[t][j].data_ptr() for t in range(3) for j in range(world)]
+    for r in range(world):
+        h3b.int8_mm_scaled_a2a(xq[r], w, xs[r], ws, bias, dst, starts[r], D, DH, hp, world, norm_w=nw, norm_eps=1e-6)
+    outs = []
+    for r in range(world):
+        y = h3b.int8_mm_scaled(xq[r], w, xs[r], ws, bias=bias).view(-1, 3, heads, DH)
+        q = F.rms_norm(y[:, 0], (DH,), nw[0], 1e-6)
+        k = F.rms_norm(y[:, 1], (DH,), nw[1], 1e-6)
+        outs.append([q, k, y[:, 2]])
+    torch.cuda.synchronize()
+    assert h3b.status() == 0
+    for t in range(3):
+        ref = sp_layout.a2a_fwd([bits(o[t].contiguous()) for o in outs], world)
+        for j in range(world):
+            np.testing.assert_array_equal(bits(recv[t][j]).reshape(S, hp, DH), ref[j], err_msg=f"t={t} j={j}")
+
+
 def test_peer_barrier_times_out_and_reports():
     """A barrier whose peer never arrives gives up after its limit and records
     STATUS_PEER_TIMEOUT; the context stays usable and an arrived barrier passes."""

@@ -78,3 +78,8 @@ def test_host_pipeline_matches_serial_steps():
     for k in range(5):
         ref = dit.forward(xs[k].to(DEV), ridx).cpu()
         assert torch.equal(outs[k].view(torch.int16), ref.view(torch.int16)), f"step {k} differs"
+
+
+def test_block_with_qk_norm():
+    """The block with the per-head q/k RMSNorm (rms_norm kernel on the unfused path)."""
+    _run(hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816, qk_norm=True), S=1000, R=2, seed=6)

@@ -124,6 +124,14 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize(dev)
         bad = (y3.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
         assert bad == 0, f"unfused-exchange block at world {world}: {bad} elements differ"
+        # a block with the per-head q/k norm: fused into the qkv GEMM's epilogue here
+        cfg_n = hm.DiTConfig(qk_norm=True)
+        p_n = hm.make_params(cfg_n, 0, 8, dev, R=2)
+        y4 = hm.block_forward(cfg_n, p_n, x.clone(), ridx, ctx)
+        y4_ref = tp.block_forward(cfg_n, p_n, x.clone(), ridx, h3b.SPContext(rank, world, g, S))
+        torch.cuda.synchronize(dev)
+        bad = (y4.view(torch.int16) != y4_ref.view(torch.int16)).sum().item()
+        assert bad == 0, f"qk-norm block at world {world}: {bad} elements differ"
         # the same block with the exchange/attention overlap (one head per group)
         y2 = hm.block_forward(cfg, p, x.clone(), ridx, ctx, overlap_groups=cfg.heads // world)
         torch.cuda.synchronize(dev)
