@@ -383,6 +383,10 @@ def breakdown(spans, pk):
         if d["ms"] > 0 and d["work"] > 0:
             if name.startswith("gemm"):
                 item["achieved_tops"] = round(d["work"] / (d["ms"] * 1e-3) / 1e12, 1)
+            elif name == "sdpa":  # PyTorch's attention kernel (not this library's), bf16 tensor flops
+                tf = d["work"] / (d["ms"] * 1e-3) / 1e12
+                item["achieved_tflops"] = round(tf, 1)
+                item["bf16_sustained_frac"] = round(tf / pk["bf16_tflops_sustained"], 3)
             elif name.startswith("a2a_fwd_p2p") or name.startswith("a2a_inv_p2p"):
                 item["off_rank_gbs"] = round(d["work"] / (d["ms"] * 1e-3) / 1e9, 1)
             else:

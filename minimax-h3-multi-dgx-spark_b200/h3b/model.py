@@ -41,6 +41,7 @@ from .linear import gelu_quant as _gelu_quant
 from .linear import int8_mm_scaled as _mm8
 from .linear import linear as _linear8
 from .linear import quant_rowwise as _quant
+from .trace import span
 
 BF16 = torch.bfloat16
 
@@ -123,9 +124,12 @@ def _lin_q(q, l):
 
 def sdpa(q, k, v):
     """q [Sq, h, Dh], k/v [Sk, h, Dh] (any row strides) -> [Sq, h, Dh] (a strided view of
-    SDPA's [1, h, Sq, Dh] output) via SDPA on [1, h, S, Dh] views."""
-    o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
-                                       v.transpose(0, 1).unsqueeze(0))
+    SDPA's [1, h, Sq, Dh] output) via SDPA on [1, h, S, Dh] views (PyTorch's own
+    kernel, as in the reference; traced as "sdpa" with its 4*Sq*Sk*h*Dh flops)."""
+    sq, h, dh = q.shape
+    with span("sdpa", 4.0 * sq * k.shape[0] * h * dh, launches=0):
+        o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0),
+                                           v.transpose(0, 1).unsqueeze(0))
     return o.squeeze(0).transpose(0, 1)
 
 
