@@ -106,4 +106,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("H3_REFERENCE_ROOT", "/root/reference"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("H3_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference project root> (or set H3_REFERENCE_ROOT)")
+    main(root)
