@@ -410,13 +410,25 @@ class CpuReference:
     ms per step."""
 
     def __init__(self, cfg, seq, rows=1024, q_rows=256):
-        from h3b import model as hm
+        from types import SimpleNamespace as NS
+
+        from oracle import torch_path as tp
 
         torch.set_num_threads(os.cpu_count() or 1)
         self.cfg, self.seq, self.rows, self.q_rows = cfg, seq, rows, q_rows
         g = torch.Generator().manual_seed(5)
         D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
-        self.p = hm.make_params(hm.DiTConfig(dim=D, heads=H, head_dim=Dh, ffn=cfg.ffn), 0, 1, torch.device("cpu"))
+
+        def lin(n, k):  # random-init INT8 linear of the benchmark block (same distributions as the GPU arm)
+            return NS(w=torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8),
+                      ws=(torch.rand(n, generator=g) + 0.5) / (127.0 * k ** 0.5),
+                      b=(torch.randn(n, generator=g) * 0.02).to(torch.bfloat16))
+
+        e = (0.1 * torch.randn(1, 6, D, generator=g)).to(torch.bfloat16)
+        self.p = NS(n1w=(1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16),
+                    n2w=(1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16),
+                    qkv=lin(3 * D, D), out=lin(D, D), up=lin(cfg.ffn, D), down=lin(D, cfg.ffn),
+                    tables=tp.modulation_tables(*(e[:, i] for i in range(6))))
         self.x = torch.randn(rows, D, generator=g).to(torch.bfloat16)
         self.ridx = torch.zeros(rows, dtype=torch.int32)
         self.q = torch.randn(q_rows, H, Dh, generator=g).to(torch.bfloat16)
@@ -589,9 +601,10 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        from h3b import model as hm
+        from types import SimpleNamespace
         seq = args.seq or 128000
-        cfg = hm.DiTConfig()
+        # the benchmark block's shape (the reference arm loads nothing of this library)
+        cfg = SimpleNamespace(dim=5120, heads=40, head_dim=128, ffn=13824, eps=1e-6)
         ref = CpuReference(cfg, seq)
         for _ in range(args.warmup):
             ref.run()

@@ -64,6 +64,13 @@ def gate_norm_mod_(x, o, g, w, eps, ridx, s1, sh):
     return norm_mod(x, w, eps, ridx, s1, sh)
 
 
+def modulation_tables(shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp):
+    """adaLN vectors -> bf16 tables (s1a, sha, ga, s1m, shm, gm), s1 = bf16(1.0 + bf16(scale))
+    (h3_fuse_patch.py:111-118, evaluated with PyTorch as the reference does)."""
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    return (1.0 + bf(scale_msa)), bf(shift_msa), bf(gate_msa), (1.0 + bf(scale_mlp)), bf(shift_mlp), bf(gate_mlp)
+
+
 def a2a_gather_seq_scatter_heads(t, ctx):
     s_local, heads, dim = t.shape
     p = ctx.world
