@@ -54,3 +54,30 @@ def test_python_binding_signatures_cover_header():
     from h3b import _lib
     bound = {name for name, _, _ in _lib.SIGNATURES}
     assert set(declared()) <= bound
+
+
+def test_entry_points_reject_bad_arguments_before_any_device_work():
+    """Argument checks run on the host before any CUDA call: a NULL pointer or an
+    unsupported shape returns H3B_ERR_ARG (-1) with a message naming the entry
+    point (the GEMM's checks name "h3b GEMM"), on a machine without a GPU too
+    (the error behaviour a caller binds to)."""
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "minimax-h3-multi-dgx-spark_b200"))
+    from h3b._lib import lib
+    p0 = ctypes.c_void_p(0)
+    cases = [
+        ("h3b_quant_rowwise", lambda: lib.h3b_quant_rowwise(p0, 64, 4, 64, p0, p0, p0)),
+        ("h3b_quant_rowwise_convrot", lambda: lib.h3b_quant_rowwise_convrot(p0, 256, 4, 256, 128, p0, p0, p0)),
+        ("h3b_int8_mm_scaled", lambda: lib.h3b_int8_mm_scaled(p0, p0, p0, p0, p0, p0, 4, 8, 100, p0)),
+        ("h3b_norm_mod", lambda: lib.h3b_norm_mod(p0, p0, 1e-6, p0, p0, p0, p0, 4, 64, 1, p0)),
+        ("h3b_rms_norm", lambda: lib.h3b_rms_norm(p0, p0, 1e-6, p0, 4, 64, p0)),
+        ("h3b_a2a_pack", lambda: lib.h3b_a2a_pack(p0, 64, p0, 4, 32, 32, 2, p0)),
+        ("h3b_a2a_inv_quant", lambda: lib.h3b_a2a_inv_quant(None, 64, 0, 4, 32, 2, p0, p0, p0)),
+        ("h3b_peer_barrier", lambda: lib.h3b_peer_barrier(None, 9, 0, 1, 1000, p0)),
+        ("h3b_int8_linear_noalloc", lambda: lib.h3b_int8_linear_noalloc(p0, 70000, 128, p0, p0, p0, 8, p0, p0)),
+    ]
+    for name, call in cases:
+        rc = call()
+        assert rc == -1, f"{name} returned {rc}"
+        msg = lib.h3b_last_error().decode()
+        assert name in msg or ("mm_scaled" in name and "GEMM" in msg), f"{name}: unexpected message {msg!r}"
