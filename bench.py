@@ -65,6 +65,7 @@ def parse_args():
     ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a"],
                     default="dit_block")
     ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
+    ap.add_argument("--qknorm", action="store_true", help="qkv_a2a workload: with the per-head q/k RMSNorm")
     ap.add_argument("--convrot", type=int, default=0, choices=[0, 64, 256],
                     help="linear workload: ConvRot quantiser with this rotation group (0 = plain)")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
@@ -525,9 +526,11 @@ def qkv_a2a_workload(args, dev):
     dst = [t.data_ptr() for t in recv]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    nw = (1 + 0.02 * torch.randn(2, Dh, generator=g)).to(torch.bfloat16).to(dev) if args.qknorm else None
+
     def step():
         flush.zero_()
-        h3b.int8_mm_scaled_a2a(xq, w, xs, ws, b, dst, 0, D, Dh, hp, P)
+        h3b.int8_mm_scaled_a2a(xq, w, xs, ws, b, dst, 0, D, Dh, hp, P, norm_w=nw)
 
     def step_plain():
         flush.zero_()
@@ -669,6 +672,7 @@ def main():
                     "unit": "TOPS", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "int8",
                     "config": {"workload": "qkv_a2a", "M": M, "N": 3 * 5120, "K": 5120, "peers_emulated": args.peers,
+                               "qk_norm": args.qknorm,
                                "l2": "256 MB flush per step"},
                     "roofline": {"kernel": "gemm_i8_pair_kernel<false, SCATTER> (tcgen05 cta_group::2 kind::i8 + "
                                            "scatter epilogue)", "bound": "tensor", "achieved": round(ach, 1),
