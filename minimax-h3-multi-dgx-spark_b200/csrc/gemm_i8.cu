@@ -325,7 +325,8 @@ __device__ __forceinline__ void scatter_head_norm(const Args& args, uint4* stage
 #pragma unroll
         for (int vt = 0; vt < off; ++vt) part[vt] = __fadd_rn(part[vt], part[vt + off]);
     const float tot = __fadd_rn(__fadd_rn(part[0], 0.0f), __fadd_rn(0.0f, 0.0f));
-    const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(tot, 128.0f), args.sc.norm_eps));
+    // tot / 128: a multiply by 2^-7 rounds the same exact quotient as the division
+    const float rstd = rsqrtf(__fadd_rn(__fmul_rn(tot, 0.0078125f), args.sc.norm_eps));
     const uint4* wv = reinterpret_cast<const uint4*>(w);
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
