@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload dit_block|dit_step|linear|fused|a2a|qkv_a2a] [--seq S] [--exchange p2p|nccl]
-                    [--overlap G]
+                    [--overlap G] [--rows M] [--blocks B] [--convrot 64|256] [--qknorm] [--peers P]
 
 Default workload (dit_block): one synthetic DiT block of the benchmark's
 block configuration -- D=5120, 40 heads x 128, FFN 13824 (GELU-tanh), four
