@@ -115,6 +115,18 @@ H3B_API int h3b_gelu_quant(const void *u, int64_t ldu, int64_t M, int64_t K, int
 H3B_API int h3b_int8_mm_scaled(const int8_t *xq, const int8_t *w, const float *xs, const float *ws, const void *bias,
                        void *out, int64_t M, int64_t N, int64_t K, void *stream);
 
+/* h3b_int8_mm_scaled with the GELU (tanh) of the FFN in the epilogue:
+ * out[m,n] = bf16(gelu(y)), y = the bf16 value h3b_int8_mm_scaled would store,
+ * gelu in PyTorch's fp32 formula (x^3 as (x*x)*x, inner = kBeta * fma(kKappa,
+ * x^3, x), 0.5*x*(1 + tanhf(inner))), each operation rounded once -- equal to
+ * F.gelu(h3b_int8_mm_scaled(...), approximate="tanh") bit for bit, without the
+ * pre-activation reaching memory.  The up projection + activation of the
+ * block's MLP (comfyui_nodes/h3-fuse-graph/h3_fuse_kernels.py:3-7, mlp_out; the
+ * reference's checkpoint fuses its SwiGLU into the next quantiser instead,
+ * h3_linear_fast_patch.py:63). */
+H3B_API int h3b_int8_mm_scaled_gelu(const int8_t *xq, const int8_t *w, const float *xs, const float *ws,
+                                    const void *bias, void *out, int64_t M, int64_t N, int64_t K, void *stream);
+
 /* Same GEMM writing the raw int32 accumulators acc [M,N] (the value the
  * reference kernel's tl.dot produces, int8_gemm_triton.py:54-60). */
 H3B_API int h3b_int8_mm_i32(const int8_t *xq, const int8_t *w, int32_t *acc, int64_t M, int64_t N, int64_t K,

@@ -27,6 +27,7 @@
 #include <stdlib.h>
 
 #include "common.cuh"
+#include "quant_common.cuh"  // gelu2
 
 namespace h3b {
 namespace gemm {
@@ -82,6 +83,7 @@ struct Args {
     int* status;
     int tile_n;  // 2-CTA kernel: output tile width (multiple of 32, <= 256)
     Scatter sc;  // scatter epilogue only
+    int act;     // bf16 output: 1 = GELU(tanh) applied to each rounded output value
 };
 
 // ---------------------------------------------------------------------------
@@ -236,7 +238,9 @@ __device__ __forceinline__ void store_chunk(const Args& args, const uint32_t (&r
         for (int g = 0; g < 4; ++g) {
             const int cb = col0 + 8 * g;
             if (cb >= N) break;
-            dst[g] = dequant8(args, r + 8 * g, cb, xs);
+            uint4 y = dequant8(args, r + 8 * g, cb, xs);
+            if (args.act) y = make_uint4(gelu2(y.x), gelu2(y.y), gelu2(y.z), gelu2(y.w));
+            dst[g] = y;
         }
     }
 }
@@ -971,6 +975,14 @@ extern "C" int h3b_int8_mm_scaled(const int8_t* xq, const int8_t* w, const float
                                   const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
     H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_scaled: shape out of range");
     gemm::Args a{xs, ws, static_cast<const uint16_t*>(bias), out, (int)M, (int)N, (int)K, nullptr};
+    return gemm::launch<false>(xq, w, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_int8_mm_scaled_gelu(const int8_t* xq, const int8_t* w, const float* xs, const float* ws,
+                                       const void* bias, void* out, int64_t M, int64_t N, int64_t K, void* stream) {
+    H3B_REQUIRE(fits_int(M) && fits_int(N) && fits_int(K), "h3b_int8_mm_scaled_gelu: shape out of range");
+    gemm::Args a{xs, ws, static_cast<const uint16_t*>(bias), out, (int)M, (int)N, (int)K, nullptr};
+    a.act = 1;
     return gemm::launch<false>(xq, w, a, static_cast<cudaStream_t>(stream));
 }
 

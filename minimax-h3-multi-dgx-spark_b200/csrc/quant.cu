@@ -28,24 +28,6 @@ namespace h3b {
 
 enum class Act { kNone = 0, kGeluTanh = 1 };
 
-// bf16(gelu_tanh(x)) of two elements: PyTorch's GeluCUDAKernelImpl formula in
-// fp32, x^3 as (x*x)*x, inner = kBeta * fma(kKappa, x^3, x), 0.5*x*(1+tanhf(inner)),
-// each operation rounded once, on fp32 pairs (f32x2 instructions round each
-// lane exactly as the scalar ones).
-__device__ __forceinline__ uint32_t gelu2(uint32_t v) {
-    constexpr float kBeta = (float)(1.41421356237309504880 * 1.12837916709551257390 * 0.5);
-    constexpr float kKappa = (float)0.044715;
-    const uint64_t x = f2(bf16_lo(v), bf16_hi(v));
-    const uint64_t x3 = mul2(mul2(x, x), x);
-    const uint64_t inner = mul2(f2(kBeta, kBeta), fma2(f2(kKappa, kKappa), x3, x));
-    float i0, i1;
-    f2_split(inner, i0, i1);
-    const uint64_t t1 = add2(f2(1.0f, 1.0f), f2(tanhf(i0), tanhf(i1)));
-    float y0, y1;
-    f2_split(mul2(mul2(f2(0.5f, 0.5f), x), t1), y0, y1);
-    return pack_bf16x2(y0, y1);
-}
-
 constexpr int kMaxGatherRanks = 8;
 
 // Row source of the inverse-exchange quantiser: vector j of local row m is

@@ -28,6 +28,7 @@ SIGNATURES = [
     ("h3b_quant_rowwise_convrot", _I32, [_P, _I64, _I64, _I64, _I64, _P, _P, _P]),
     ("h3b_swiglu_quant_convrot", _I32, [_P, _I64, _I64, _I64, _I64, _P, _P, _P]),
     ("h3b_int8_mm_scaled", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    ("h3b_int8_mm_scaled_gelu", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_int8_mm_i32", _I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_int8_mm_scaled_a2a", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _PP, _I64, _I64, _I64, _I64, _I32, _P]),
     ("h3b_int8_mm_scaled_a2a_qknorm", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _PP, _I64, _I64, _I64, _I64, _I32,

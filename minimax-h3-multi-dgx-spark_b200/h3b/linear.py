@@ -100,10 +100,11 @@ def _gemm_checks(xq, w):
     return M, N, K
 
 
-def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
+def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None, act=None):
     """xq [M,K] int8, w [N,K] int8, xs [M,1] fp32, ws [N] fp32 -> [M,N] bf16.
 
-    out = bf16((float(xq @ w.T) * xs) * ws [+ bias]) with one rounding."""
+    out = bf16((float(xq @ w.T) * xs) * ws [+ bias]) with one rounding; with
+    act="gelu", F.gelu(out, approximate="tanh") computed in the epilogue."""
     M, N, K = _gemm_checks(xq, w)
     xs = xs.reshape(-1)
     if xs.dtype != torch.float32 or ws.dtype != torch.float32 or xs.numel() != M or ws.numel() != N:
@@ -115,9 +116,12 @@ def int8_mm_scaled(xq, w, xs, ws, out=None, bias=None):
         bias = bias.contiguous()
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=xq.device)
+    if act not in (None, "gelu"):
+        raise ValueError(f"int8_mm_scaled: unknown act {act!r}")
+    fn = lib.h3b_int8_mm_scaled_gelu if act == "gelu" else lib.h3b_int8_mm_scaled
     with span("gemm", 2 * M * N * K):
-        check(lib.h3b_int8_mm_scaled(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
-              "h3b_int8_mm_scaled")
+        check(fn(ptr(xq), ptr(w), ptr(xs), ptr(ws), ptr(bias), ptr(out), M, N, K, stream_of(xq)),
+              "h3b_int8_mm_scaled_gelu" if act else "h3b_int8_mm_scaled")
     return out
 
 

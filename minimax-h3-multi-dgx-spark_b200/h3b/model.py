@@ -202,6 +202,10 @@ FUSED_EXCHANGE = os.environ.get("H3B_FUSED_EXCHANGE", "1") != "0"
 # faster form as measured in the block.
 FUSED_NORM_QUANT = os.environ.get("H3B_FUSED_NORM_QUANT", "0") == "1"
 FUSED_GELU_QUANT = os.environ.get("H3B_FUSED_GELU_QUANT", "1") == "1"
+# The GELU can instead run in the up projection's epilogue (the GEMM writes
+# gelu(u), the plain quantiser follows); H3B_GELU_EPILOGUE=1 selects it and it
+# takes precedence over FUSED_GELU_QUANT.
+GELU_EPILOGUE = os.environ.get("H3B_GELU_EPILOGUE", "0") == "1"
 
 
 def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, overlap_groups=None):
@@ -222,10 +226,14 @@ def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, ov
     else:
         hq = _quant(fuse.gate_norm_mod_(x, o, ga, p.n2w, cfg.eps, ridx, s1m, shm))
     del o
-    u = _lin_q(hq, p.up)
-    del hq
-    aq = _gelu_quant(u) if fused_gelu else _quant(F.gelu(u, approximate="tanh"))
-    del u
+    if GELU_EPILOGUE and fused_producers is None:
+        aq = _quant(_mm8(hq[0], p.up.w, hq[1], p.up.ws, bias=p.up.b, act="gelu"))
+        del hq
+    else:
+        u = _lin_q(hq, p.up)
+        del hq
+        aq = _gelu_quant(u) if fused_gelu else _quant(F.gelu(u, approximate="tanh"))
+        del u
     m = _lin_q(aq, p.down)
     del aq
     fuse.gate_(x, m, gm, ridx)

@@ -235,3 +235,18 @@ def test_gemm_rows_independent_of_m():
     for lo, hi in ((0, 100), (0, 129), (1000, 1516), (3000, 4128), (7, 8)):
         part = h3b.linear(x[lo:hi].to(DEV), wd, wsd, bd)
         assert torch.equal(part.view(torch.int16), full[lo:hi].view(torch.int16)), (lo, hi)
+
+
+@pytest.mark.parametrize("M,N,K", [(513, 13824, 5120), (100, 2048, 1024), (4096, 5120, 256)])
+def test_gemm_gelu_epilogue_equals_torch_gelu(M, N, K):
+    """GELU in the GEMM epilogue == F.gelu of the plain GEMM's bf16 output, bit for bit."""
+    import torch.nn.functional as F
+    g = gen(M + N + K + 5)
+    xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(DEV)
+    w, ws, bias = _weights(N, K, seed=N + 7)
+    xs = (torch.rand(M, 1, generator=g) * 0.05 + 1e-3).to(DEV)
+    wd, wsd, bd = w.to(DEV), (ws * 40).to(DEV), bias.to(DEV)
+    y = h3b.int8_mm_scaled(xq, wd, xs, wsd, bias=bd, act="gelu")
+    ref = F.gelu(h3b.int8_mm_scaled(xq, wd, xs, wsd, bias=bd), approximate="tanh")
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), f"{(y != ref).sum().item()} elements differ"
