@@ -218,7 +218,7 @@ def test_gemm_a2a_qknorm_emulated(world, S, heads, K):
     F.rms_norm applied (on the GPU, per 128-wide head) to the unfused GEMM's q and
     k; v passes through unnormalised."""
     import torch.nn.functional as F
-    from gpu_util import adversarial_rows, gen
+    from gpu_util import gen
     splits = sp_layout.splits(S, world)
     starts = sp_layout.starts(S, world)
     hp = heads // world
