@@ -7,6 +7,8 @@ Drop-in replacements for the three hooks of yuichi-suzuki-highdrama/minimax-h3-m
 All compute runs in libh3b.so (hand-written CUDA for sm_100a, C ABI in
 include/h3b.h); this package is the host-side mirror of the reference's
 operator interfaces.  Importing it fails if the library is not built.
+h3b.model holds the synthetic DiT block / step that drives the path in the
+benchmark and HostPipeline, the host-latent runner.
 """
 from ._lib import H3BError, clear_status, lib, status  # noqa: F401
 from .fuse import (gate_, gate_norm_mod_, gate_norm_mod_quant_, modulation_tables, norm_mod,  # noqa: F401

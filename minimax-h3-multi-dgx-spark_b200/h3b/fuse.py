@@ -7,6 +7,9 @@ Kernel-level API of comfyui_nodes/h3-fuse-graph/h3_fuse_kernels.py:174-192:
 plus the per-forward helpers of comfyui_nodes/h3-fuse-graph/h3_fuse_patch.py:
   row_index(mod_segments, s, device)   :32-56
   modulation_tables(vecs)              :111-118
+the producers that also quantise their output for the INT8 linear they feed
+(norm_mod_quant, gate_norm_mod_quant_), and the plain RMSNorm of the per-head
+q/k norm (rms_norm, comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:296-298).
 """
 import torch
 
