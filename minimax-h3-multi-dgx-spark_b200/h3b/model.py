@@ -151,7 +151,7 @@ def self_attention(cfg, p, hq, ctx, overlap_groups=None):
     hp = H // ctx.world if sharded else H
     n = (sp.overlap_groups(hp, ctx.world) if overlap_groups is None else overlap_groups) if sharded else 0
     overlap = n > 1 and hp % n == 0
-    if sharded and not overlap and ctx.exchange == "p2p" and FUSED_EXCHANGE:
+    if sharded and not overlap and sp._p2p(ctx) is not None and FUSED_EXCHANGE:
         # the qkv GEMM's epilogue (with the q/k norms when the block has them)
         # stores q, k, v straight into the owners' buffers; the out projection's
         # quantiser gathers its rows from every rank's output

@@ -55,6 +55,13 @@ class SPContext:
         return self.splits[self.rank]
 
 
+def _p2p(ctx):
+    """The PeerExchange of ctx when it selects the peer-memory back end, else None.
+    A context without these attributes (the reference's own SPContext,
+    sp_forward.py:140-155, passed by a patched caller) uses NCCL."""
+    return ctx.peer if getattr(ctx, "exchange", "nccl") == "p2p" else None
+
+
 # ---------------------------------------------------------------------------
 # NCCL back end (pure torch.distributed; also runs on gloo/CPU for host tests)
 
@@ -130,7 +137,7 @@ def a2a_gather_seq_scatter_heads(t, ctx):
     """[s_local, H, D] -> [S_total, H/P, D]."""
     s_local, heads, dim = t.shape
     hp = heads // ctx.world
-    if ctx.exchange == "p2p":
+    if _p2p(ctx):
         return ctx.peer.fwd([t], ctx)[0]
     send = pack(t, ctx.world).view(-1)
     out = torch.empty(ctx.seq_len * hp * dim, dtype=t.dtype, device=t.device)
@@ -141,7 +148,7 @@ def a2a_gather_seq_scatter_heads(t, ctx):
 def a2a_gather_qkv(q, k, v, ctx):
     """The three forward exchanges of one attention call at once (one launch /
     one NCCL group instead of three)."""
-    if ctx.exchange == "p2p":
+    if _p2p(ctx):
         return ctx.peer.fwd([q, k, v], ctx)
     s_local, heads, dim = q.shape
     hp = heads // ctx.world
@@ -158,7 +165,7 @@ def a2a_gather_qkv(q, k, v, ctx):
 
 def a2a_scatter_seq_gather_heads(t, ctx):
     """[S_total, (H/P)*D] -> [s_local, H*D]."""
-    if ctx.exchange == "p2p":
+    if _p2p(ctx):
         return ctx.peer.inv(t, ctx)
     chunk = t.shape[1]
     out = torch.empty(ctx.world * ctx.local * chunk, dtype=t.dtype, device=t.device)
@@ -197,7 +204,7 @@ def sp_attention_overlap(q, k, v, ctx, attn, groups):
     hp = heads // ctx.world
     if groups < 1 or hp % groups:
         raise ValueError(f"{groups} groups do not divide the {hp} heads of a rank")
-    if ctx.exchange == "p2p":
+    if _p2p(ctx):
         return ctx.peer.attention_overlap(q, k, v, ctx, attn, groups)
     P, hc = ctx.world, hp // groups
     w = hc * dim
