@@ -404,19 +404,23 @@ def breakdown(spans, pk):
 class CpuReference:
     """The reference's eager PyTorch path on the host cores, on a bounded sample.
 
-    Row-local work (norms, INT8 linears, GELU, gates) runs on `rows` rows and is
-    scaled by seq/rows; attention runs for `q_rows` query rows against all `seq`
-    keys/values of every head and is scaled by seq/q_rows.  Set-up (weights,
-    inputs) happens once; run() times one sample and returns the extrapolated
-    ms per step."""
+    Row-local work (norms, INT8 linears, GELU, gates) is timed on rows_lo and
+    rows_hi rows and attention on q_lo and q_hi query rows against all `seq`
+    keys/values of every head; each part is extrapolated to the full sequence by
+    the straight line through its two points (a fixed cost -- the layout copies
+    of K and V inside SDPA, thread start-up -- plus a cost per row), so the
+    fixed costs are counted once, not once per sampled fraction.  Set-up
+    (weights, inputs) happens once; run() times one sample and returns the
+    extrapolated ms per step."""
 
-    def __init__(self, cfg, seq, rows=1024, q_rows=256):
+    def __init__(self, cfg, seq, rows=(512, 2048), q_rows=(1024, 4096)):
         from types import SimpleNamespace as NS
 
         from oracle import torch_path as tp
 
         torch.set_num_threads(os.cpu_count() or 1)
-        self.cfg, self.seq, self.rows, self.q_rows = cfg, seq, rows, q_rows
+        self.cfg, self.seq = cfg, seq
+        self.rows, self.q_rows = tuple(min(r, seq) for r in rows), tuple(min(q, seq) for q in q_rows)
         g = torch.Generator().manual_seed(5)
         D, H, Dh = cfg.dim, cfg.heads, cfg.head_dim
 
@@ -430,46 +434,60 @@ class CpuReference:
                     n2w=(1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16),
                     qkv=lin(3 * D, D), out=lin(D, D), up=lin(cfg.ffn, D), down=lin(D, cfg.ffn),
                     tables=tp.modulation_tables(*(e[:, i] for i in range(6))))
-        self.x = torch.randn(rows, D, generator=g).to(torch.bfloat16)
-        self.ridx = torch.zeros(rows, dtype=torch.int32)
-        self.q = torch.randn(q_rows, H, Dh, generator=g).to(torch.bfloat16)
+        self.x = torch.randn(max(self.rows), D, generator=g).to(torch.bfloat16)
+        self.ridx = torch.zeros(max(self.rows), dtype=torch.int32)
+        self.q = torch.randn(max(self.q_rows), H, Dh, generator=g).to(torch.bfloat16)
         self.k = torch.randn(seq, H, Dh, generator=g).to(torch.bfloat16)
         self.v = torch.randn(seq, H, Dh, generator=g).to(torch.bfloat16)
 
-    def _rowwork(self):
+    def _rowwork(self, n):
         import torch.nn.functional as F
 
         from oracle import torch_path as tp
         p, cfg, D = self.p, self.cfg, self.cfg.dim
         s1a, sha, ga, s1m, shm, gm = p.tables
-        xx = self.x.clone()
-        h = tp.norm_mod(xx, p.n1w, cfg.eps, self.ridx, s1a, sha)
+        xx, ridx = self.x[:n].clone(), self.ridx[:n]
+        h = tp.norm_mod(xx, p.n1w, cfg.eps, ridx, s1a, sha)
         qkv = tp.linear(h, p.qkv.w, p.qkv.ws, p.qkv.b)
         o = tp.linear(qkv[:, :D], p.out.w, p.out.ws, p.out.b)  # out-proj on an attention-output-sized input
-        h = tp.gate_norm_mod_(xx, o, ga, p.n2w, cfg.eps, self.ridx, s1m, shm)
+        h = tp.gate_norm_mod_(xx, o, ga, p.n2w, cfg.eps, ridx, s1m, shm)
         u = tp.linear(h, p.up.w, p.up.ws, p.up.b)
         m = tp.linear(F.gelu(u, approximate="tanh"), p.down.w, p.down.ws, p.down.b)
-        tp.gate_(xx, m, gm, self.ridx)
+        tp.gate_(xx, m, gm, ridx)
 
-    def _attn(self):
+    def _attn(self, n):
         from oracle import torch_path as tp
-        tp.sdpa_heads(self.q, self.k, self.v)
+        tp.sdpa_heads(self.q[:n], self.k, self.v)
+
+    @staticmethod
+    def _timed(fn, n):
+        t0 = time.perf_counter()
+        fn(n)
+        return time.perf_counter() - t0
+
+    def _line(self, fn, lo, hi):
+        """Seconds for the full sequence from the line through (lo, t_lo) and (hi, t_hi)."""
+        t_lo, t_hi = self._timed(fn, lo), self._timed(fn, hi)
+        self.last_cpu_s += t_lo + t_hi
+        if hi <= lo:
+            return t_hi * self.seq / hi
+        per_row = (t_hi - t_lo) / (hi - lo)
+        if per_row <= 0.0:  # timing noise swamped the slope: plain proportional scaling (an upper bound)
+            return t_hi * self.seq / hi
+        return max(t_hi - per_row * hi, 0.0) + per_row * self.seq
 
     def run(self):
-        t0 = time.perf_counter()
-        self._rowwork()
-        t_rows = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        self._attn()
-        t_attn = time.perf_counter() - t0
-        self.last_cpu_s = t_rows + t_attn
-        return (t_rows * self.seq / self.rows + t_attn * self.seq / self.q_rows) * 1e3
+        self.last_cpu_s = 0.0
+        rows_s = self._line(self._rowwork, *self.rows)
+        attn_s = self._line(self._attn, *self.q_rows)
+        return (rows_s + attn_s) * 1e3
 
     def sample(self):
         return (f"eager PyTorch CPU path (oracle/torch_path.py): row-local block work (norms, 4 INT8 linears, "
-                f"GELU, gates) on {self.rows} of {self.seq} rows (x{self.seq / self.rows:.1f}) + SDPA for "
-                f"{self.q_rows} query rows vs all {self.seq} keys, {self.cfg.heads} heads "
-                f"(x{self.seq / self.q_rows:.1f}); {self.last_cpu_s:.1f} s of CPU work per sample")
+                f"GELU, gates) on {self.rows[0]} and {self.rows[1]} of {self.seq} rows, SDPA for {self.q_rows[0]} "
+                f"and {self.q_rows[1]} query rows vs all {self.seq} keys, {self.cfg.heads} heads; each part "
+                f"extrapolated to {self.seq} rows along the line through its two timings (fixed cost counted "
+                f"once); {self.last_cpu_s:.1f} s of CPU work per sample")
 
 
 def cpu_baseline(cfg, seq, steps=3, warmup=1):
