@@ -413,7 +413,7 @@ class CpuReference:
     (weights, inputs) happens once; run() times one sample and returns the
     extrapolated ms per step."""
 
-    def __init__(self, cfg, seq, rows=(512, 2048), q_rows=(1024, 4096)):
+    def __init__(self, cfg, seq, rows=(1024, 4096), q_rows=(2048, 8192)):
         from types import SimpleNamespace as NS
 
         from oracle import torch_path as tp
