@@ -250,3 +250,23 @@ def test_gemm_gelu_epilogue_equals_torch_gelu(M, N, K):
     ref = F.gelu(h3b.int8_mm_scaled(xq, wd, xs, wsd, bias=bd), approximate="tanh")
     torch.cuda.synchronize()
     assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), f"{(y != ref).sum().item()} elements differ"
+
+
+@pytest.mark.parametrize("N,K", [(15360, 5120), (5120, 13824)])
+def test_gemm_full_block_size_vs_cublas(N, K):
+    """The block's qkv and down projections at the benchmark's full M=128000:
+    int32 sums equal cuBLAS's torch._int_mm, bf16 outputs equal the fp32 formula."""
+    M = 128000
+    g = gen(N + K)
+    xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(DEV)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(DEV)
+    xs = (torch.rand(M, 1, generator=g) * 0.05 + 1e-3).to(DEV)
+    ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(DEV)
+    ref_acc = torch._int_mm(xq, w.t())
+    acc = h3b.int8_mm_i32(xq, w)
+    assert torch.equal(acc, ref_acc)
+    del acc
+    y = h3b.int8_mm_scaled(xq, w, xs, ws)
+    ref = ((ref_acc.float() * xs) * ws).to(torch.bfloat16)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    assert h3b.status() == 0
