@@ -62,7 +62,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a"],
+    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a", "quant"],
                     default="dit_block")
     ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
     ap.add_argument("--qknorm", action="store_true", help="qkv_a2a workload: with the per-head q/k RMSNorm")
@@ -70,13 +70,18 @@ def parse_args():
                     help="linear workload: ConvRot quantiser with this rotation group (0 = plain)")
     ap.add_argument("--seq", type=int, default=None, help="sequence length (default per workload)")
     ap.add_argument("--blocks", type=int, default=None, help="blocks for dit_step (default 40)")
-    ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / S of the fused workload")
+    ap.add_argument("--rows", type=int, default=None, help="rows M of the linear / quant / S of the fused workload")
+    ap.add_argument("--cols", type=int, default=None, help="columns K of the quant workload")
+    ap.add_argument("--act", choices=["none", "gelu"], default="none", help="quant workload: activation")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default=os.environ.get("H3B_EXCHANGE", "p2p"))
     ap.add_argument("--overlap", type=int, default=None,
                     help="head groups of the exchange/attention overlap (default: H3B_SP_OVERLAP_GROUPS or the "
                          "reference's MINIMAX_SP_OVERLAP_CHUNKS; 0 = off)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the checker leg after the timed regions")
+    ap.add_argument("--no-step", action="store_true", help="dit_block: skip the 40-block step sub-record")
+    ap.add_argument("--no-a2a", action="store_true", help="dit_block at N > 1: skip the a2a sub-record")
     return ap.parse_args()
 
 
@@ -239,16 +244,40 @@ def gemm_shapes(cfg, s_local, world, exchange):
 
 
 def overlap_groups(cfg, world):
-    """Head groups the block's attention uses (0: exchange and attention in sequence)."""
+    """Head groups the block's attention uses (0: exchange and attention in sequence).
+    Reads the same environment as h3b.sp.overlap_groups without loading the
+    library (the reference arm reports the same config)."""
     if world == 1:
         return 0
-    from h3b import sp
     hp = cfg.heads // world
-    n = sp.overlap_groups(hp, world)
+
+    def env(name):
+        return int(os.environ.get(name, "0") or 0)
+    n = env("H3B_SP_OVERLAP_GROUPS") or env("MINIMAX_SP_OVERLAP_CHUNKS")
+    if world == 4:
+        n = env("MINIMAX_SP_OVERLAP_CHUNKS_W4") or n
+        while n > 1 and hp % n:
+            n -= 1
     return n if n > 1 and hp % n == 0 else 0
 
 
-def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
+def dit_config(cfg, workload, seq, world, n_blocks, text_len, exchange):
+    """The `config` object of a DiT line (both arms print the same one)."""
+    base, rem = divmod(seq, world)
+    return {"workload": workload, "seq_len": seq, "local_rows": base + (1 if rem else 0), "dim": cfg.dim,
+            "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": cfg.ffn, "blocks": n_blocks, "text_len": text_len,
+            "parallelism": f"ulysses_sp{world}", "exchange": exchange if world > 1 else None,
+            "overlap_groups": overlap_groups(cfg, world), "l2": "inputs larger than L2 (no flush)"}
+
+
+def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup, trace=True, e2e_steps=None,
+                 serial=True, parity=True, warm_blocks=0):
+    """Times `steps` forwards of an n_blocks synthetic DiT over seq tokens
+    (this rank's rows).  warmup full steps (or, with warm_blocks, that many
+    single-block forwards, which run every kernel and shape of a step) come
+    first.  Returns a dict: cfg, s_local, ms, clocks, spans/launches (trace),
+    e2e (HostPipeline, e2e_steps steps; None skips it) and parity (the
+    checker leg after all timed regions)."""
     import h3b
     from h3b import model as hm
     from h3b.trace import Trace
@@ -274,20 +303,23 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
     text = text_host.to(dev) if text_len else None
     xw = torch.empty_like(x0)
     ridx = torch.zeros(s_local, dtype=torch.int32, device=dev)
+    res = {"cfg": cfg, "s_local": s_local, "spans": {}, "launches": 0, "e2e": None, "parity": None}
 
     def step():
         xw.copy_(x0)
         dit.forward(xw, ridx, ctx, text)
 
-    ms, clocks = timed(step, args.steps, args.warmup, world, dev)
-    # per-kernel spans over a second, identical timed region (events inside it)
-    with Trace() as tr:
-        _ms2, _ = timed(step, args.steps, 0, world, dev, sample_clocks=False)
-    spans = tr.summary(args.steps)
-    launches = tr.launches / args.steps
+    for _ in range(warm_blocks):
+        xw.copy_(x0)
+        hm.block_forward(cfg, dit.params[0], xw, ridx, ctx, text)
+    res["ms"], res["clocks"] = timed(step, steps, warmup, world, dev)
+    if trace:
+        # per-kernel spans over a second, identical timed region (events inside it)
+        with Trace() as tr:
+            timed(step, steps, 0, world, dev, sample_clocks=False)
+        res["spans"], res["launches"] = tr.summary(steps), tr.launches / steps
 
-    e2e = None
-    if not args.no_e2e:
+    if e2e_steps:
         e_host = [p.e.detach().cpu().pin_memory() for p in dit.params]
 
         def load_tables():
@@ -303,32 +335,73 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len):
         def step_pipe():
             pipe.submit(x_host, outs[pipe.k % 3], before=load_tables)
 
-        ms_e2e, _ = timed(step_pipe, args.steps, 1, world, dev, sample_clocks=False, finish=pipe.flush)
+        ms_e2e, _ = timed(step_pipe, e2e_steps, 1 if serial else 0, world, dev, sample_clocks=False,
+                          finish=pipe.flush)
         del pipe
-        # serial: copy in, forward, copy out, all on the compute stream
         out_host = outs[0]
-
-        def step_serial():
-            load_tables()
-            xw.copy_(x_host, non_blocking=True)
-            y = dit.forward(xw, ridx, ctx, text)
-            out_host.copy_(y, non_blocking=True)
-
-        ms_serial, _ = timed(step_serial, args.steps, 1, world, dev, sample_clocks=False)
         h2d = x_host.numel() * 2 + sum(e.numel() * 2 for e in e_host)
         e2e = {"value": round(ms_e2e, 3), "unit": "ms/step", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": out_host.numel() * 2,
                "api": "h3b.model.HostPipeline.submit (pinned host latents in and out; copies on two copy streams "
-                      "overlap the neighbouring steps' compute, every step's copies inside the timed region)",
-               "serial_ms_per_step": round(ms_serial, 3)}
+                      "overlap the neighbouring steps' compute, every step's copies inside the timed region)"}
+        if serial:
+            # serial: copy in, forward, copy out, all on the compute stream
+            def step_serial():
+                load_tables()
+                xw.copy_(x_host, non_blocking=True)
+                y = dit.forward(xw, ridx, ctx, text)
+                out_host.copy_(y, non_blocking=True)
+
+            ms_serial, _ = timed(step_serial, e2e_steps, 1, world, dev, sample_clocks=False)
+            e2e["serial_ms_per_step"] = round(ms_serial, 3)
+        res["e2e"] = e2e
+        del outs, out_host
     status = h3b.status()
     if status:
         raise RuntimeError(f"device status {status} after the timed region")
+    if parity:
+        # xw holds the output of the last forward of x0's rows (a timed step or a serial e2e step)
+        res["parity"] = dit_parity(dit, x0, xw, ridx, text, rank, world, dev, seq, ctx)
     if peer is not None:
         torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[dev.index])
         peer.close()
-    return cfg, s_local, ms, clocks, spans, launches, e2e
+    del dit, x0, xw
+    torch.cuda.empty_cache()
+    return res
+
+
+def dit_parity(dit, x0, y, ridx, text, rank, world, dev, seq, ctx):
+    """Checker leg, run after every timed region: y, the timed path's output for
+    the step's input rows x0, against the reference's eager PyTorch path
+    (oracle/torch_path.py, which restates the eager DiTBlock sequence of
+    h3_fuse_kernels.py:3-7, the INT8 linear of int8_gemm_triton.py:2,61-66 with
+    torch._int_mm, SDPA, and at N > 1 the exchange of sp_forward.py:158-198 as
+    reshape + all_to_all_single over NCCL), same weights and rows, every block
+    of the model, compared bit for bit on every rank (mismatches summed over
+    ranks)."""
+    import h3b
+    from oracle import torch_path as tp
+
+    ctx_ref = h3b.SPContext(rank, world, dist.group.WORLD, seq) if world > 1 else None  # NCCL all_to_all_single
+    xe = x0.clone()
+    for p in dit.params:
+        xe = tp.block_forward(dit.cfg, p, xe, ridx, ctx_ref, text)
+    torch.cuda.synchronize(dev)
+    bad = (y.view(torch.int16) != xe.view(torch.int16)).sum().to(torch.float64)
+    nonfinite = (~torch.isfinite(y.float())).sum().to(torch.float64)
+    counts = torch.stack([bad, nonfinite])
+    if world > 1:
+        dist.all_reduce(counts)
+    mismatches, nonfinite = int(counts[0].item()), int(counts[1].item())
+    del xe
+    torch.cuda.empty_cache()
+    return {"block_bitexact": mismatches == 0, "mismatches": mismatches, "elements": seq * dit.cfg.dim,
+            "nonfinite": nonfinite, "blocks": len(dit.params),
+            "exchange": None if world == 1 else getattr(ctx, "exchange", "nccl"),
+            "reference": "eager PyTorch block (F.rms_norm/mul/add chain, torch._int_mm INT8 linears, SDPA"
+                         + (", reshape + all_to_all_single over NCCL)" if world > 1 else ")")
+                         + " on the same weights and rows, after the timed regions"}
 
 
 def gemm_dram_traffic(shapes):
@@ -523,6 +596,27 @@ def linear_workload(args, dev):
     return ms, clocks, tr.summary(args.steps), tr.launches / args.steps
 
 
+def quant_workload(args, dev):
+    """The activation quantiser alone (h3b_quant_rowwise, or with --act gelu the
+    GELU-tanh quantiser h3b_gelu_quant that feeds the down projection) on
+    seeded N(0,1) bf16 rows [M, K] (M*K*2 bytes > L2 at the default sizes)."""
+    import h3b
+    from h3b.trace import Trace
+    M, K = args.rows or 32768, args.cols or (13824 if args.act == "gelu" else 5120)
+    x = seeded_rows(0, M, K, seed=30).to(dev)
+    xq = torch.empty(M, K, dtype=torch.int8, device=dev)
+    xs = torch.empty(M, 1, dtype=torch.float32, device=dev)
+    fn = h3b.gelu_quant if args.act == "gelu" else h3b.quant_rowwise
+
+    def step():
+        fn(x, xq, xs)
+
+    ms, clocks = timed(step, args.steps, args.warmup, 1, dev)
+    with Trace() as tr:
+        timed(step, args.steps, 0, 1, dev, sample_clocks=False)
+    return M, K, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
+
+
 def qkv_a2a_workload(args, dev):
     """One rank's qkv projection with the forward exchange in the GEMM's epilogue
     (h3b_int8_mm_scaled_a2a), on one GPU: the P ranks' receive buffers are all
@@ -612,6 +706,86 @@ def a2a_workload(args, rank, world, dev):
     return S, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
 
 
+def nvlink_counters(dev):
+    """Cumulative NVLink bytes of this GPU from NVML (read-only counters), summed
+    over its links: {"tx": bytes, "rx": bytes, "field": name} or None.  Tries the
+    per-link byte counters, then the per-link data throughput counters (KiB)."""
+    try:
+        import pynvml as nv
+        nv.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        h = nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        links = getattr(nv, "NVML_NVLINK_MAX_LINKS", 18)
+        for name, tx_id, rx_id, scale in (
+                ("NVML_FI_DEV_NVLINK_COUNT_XMIT_BYTES/RCV_BYTES", nv.NVML_FI_DEV_NVLINK_COUNT_XMIT_BYTES,
+                 nv.NVML_FI_DEV_NVLINK_COUNT_RCV_BYTES, 1),
+                ("NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX/RX (KiB)", nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX,
+                 nv.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, 1024)):
+            ids = [(tx_id, li) for li in range(links)] + [(rx_id, li) for li in range(links)]
+            vals = nv.nvmlDeviceGetFieldValues(h, ids)
+            ok = [v.nvmlReturn == 0 for v in vals]
+            if not any(ok):
+                continue
+            tx = sum(int(v.value.ullVal) for v, o in zip(vals[:links], ok[:links]) if o) * scale
+            rx = sum(int(v.value.ullVal) for v, o in zip(vals[links:], ok[links:]) if o) * scale
+            return {"tx": tx, "rx": rx, "field": name, "links_read": sum(ok) // 2}
+    except Exception as e:  # noqa: BLE001
+        log(f"NVML NVLink counters unavailable: {e}")
+    return None
+
+
+def a2a_subrecord(args, rank, world, dev, seq=131072, steps=10, warmup=3):
+    """Configuration 2 at this world size: q, k, v [S/P, 40, 128] forward
+    exchange + inverse exchange of the received q (an identity round trip), per
+    back end; bus GB/s = 4 tensors x the per-rank buffer x (P-1)/P / time (the
+    all-to-all convention).  The round trip is checked bit for bit after the
+    timed region; NVML's NVLink byte counters are read around it."""
+    import h3b
+    H, Dh = 40, 128
+    out = {}
+    for exch in ("p2p", "nccl"):
+        peer = h3b.PeerExchange(dist.group.WORLD, rank, world, seq, H, Dh) if exch == "p2p" else None
+        ctx = h3b.SPContext(rank, world, dist.group.WORLD, seq, exchange=exch, peer=peer)
+        q, k, v = (seeded_rows(ctx.start, ctx.stop, H * Dh, seed=20 + i).to(dev).view(-1, H, Dh) for i in range(3))
+        res = {}
+
+        def step():
+            qq, kk, vv = h3b.a2a_gather_qkv(q, k, v, ctx)
+            res["back"] = h3b.a2a_scatter_seq_gather_heads(qq.reshape(seq, -1), ctx)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        c0 = nvlink_counters(dev)
+        ms, _ = timed(step, steps, 0, world, dev, sample_clocks=False)
+        c1 = nvlink_counters(dev)
+        buf = seq // world * H * Dh * 2
+        bus = 4 * buf * (world - 1) / world / (ms * 1e-3) / 1e9
+        step()
+        torch.cuda.synchronize(dev)
+        bad = (res["back"].reshape(-1).view(torch.int16) != q.reshape(-1).view(torch.int16)).sum().to(torch.float64)
+        dist.all_reduce(bad)
+        rec = {"bus_gbs": round(bus, 1), "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
+               "link_peak_gbs": 900.0, "frac_of_900": round(bus / 900.0, 3),
+               "roundtrip_bitexact": int(bad.item()) == 0, "roundtrip_mismatches": int(bad.item())}
+        if c0 and c1:
+            tx = (c1["tx"] - c0["tx"]) / steps
+            rx = (c1["rx"] - c0["rx"]) / steps
+            rec["nvml_nvlink"] = {"tx_bytes_per_step": tx, "rx_bytes_per_step": rx, "field": c0["field"],
+                                  "links_read": c0["links_read"],
+                                  "tx_gbs": round(tx / (ms * 1e-3) / 1e9, 1),
+                                  "payload_off_rank_bytes_per_step": 4 * buf * (world - 1) / world}
+        out[exch] = rec
+        if peer is not None:
+            torch.cuda.synchronize(dev)
+            dist.barrier(device_ids=[dev.index])
+            peer.close()
+        del q, k, v, res
+    torch.cuda.empty_cache()
+    return {"metric": "Ulysses a2a bus GB/s (q,k,v forward + inverse)", "unit": "GB/s",
+            "config": {"workload": "a2a", "S": seq, "heads": H, "head_dim": Dh, "world": world}, **out}
+
+
 # ---------------------------------------------------------------------------
 
 def main():
@@ -635,8 +809,8 @@ def main():
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1),
                 "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8+bf16",
                 "data": "synthetic (seeded N(0,1) activations, random-init int8 weights)",
-                "config": {"workload": "dit_block", "seq_len": seq, "dim": 5120, "heads": 40, "head_dim": 128,
-                           "ffn": 13824, "blocks": 1, "parallelism": "none (host CPU)"},
+                "config": dit_config(cfg, "dit_block", seq, args.gpus, 1, 0, args.exchange),
+                "host": "CPU (the reference's eager PyTorch path on the host cores; rank 0 only)",
                 "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": cores, "kind": "port",
                                  "sample": sample},
                 "e2e": {"value": round(v, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -650,24 +824,34 @@ def main():
             seq = args.seq or (252000 if step_cfg else 128000)
             n_blocks = args.blocks or (40 if step_cfg else 1)
             text_len = 512 if step_cfg else 0
-            cfg, s_local, ms, clocks, spans, launches, e2e = dit_workload(args, rank, world, dev, n_blocks, seq,
-                                                                          text_len)
+            r = dit_workload(args, rank, world, dev, n_blocks, seq, text_len, args.steps, args.warmup,
+                             e2e_steps=None if args.no_e2e else args.steps, parity=not args.no_parity)
+            cfg, s_local, ms, spans = r["cfg"], r["s_local"], r["ms"], r["spans"]
             line = {"metric": "DiT fwd ms/step", "value": round(ms, 3), "unit": "ms/step", "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
                     "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8+bf16",
                     "data": "synthetic (seeded N(0,1) activations, random-init int8 weights)",
-                    "config": {"workload": "dit_step" if step_cfg else "dit_block", "seq_len": seq,
-                               "local_rows": s_local, "dim": cfg.dim, "heads": cfg.heads,
-                               "head_dim": cfg.head_dim, "ffn": cfg.ffn, "blocks": n_blocks, "text_len": text_len,
-                               "parallelism": f"ulysses_sp{world}", "exchange": args.exchange if world > 1 else None,
-                               "overlap_groups": overlap_groups(cfg, world),
-                               "l2": "inputs larger than L2 (no flush)"},
+                    "config": dit_config(cfg, args.workload, seq, world, n_blocks, text_len, args.exchange),
                     "roofline": gemm_roofline(spans, pk, pk_src, gemm_shapes(cfg, s_local, world, args.exchange),
                                               in_step=True),
-                    "clocks": clocks, "e2e": e2e,
-                    "gpu_launches": int(round(launches * args.steps)), "breakdown": breakdown(spans, pk)}
+                    "clocks": r["clocks"], "e2e": r["e2e"], "parity": r["parity"],
+                    "gpu_launches": int(round(r["launches"] * args.steps)), "breakdown": breakdown(spans, pk)}
             if rank == 0 and world == 1 and not args.no_cpu_baseline and not step_cfg:
                 line["cpu_baseline"] = cpu_baseline(cfg, seq)
+            if not step_cfg and world > 1 and not args.no_a2a:
+                line["a2a"] = a2a_subrecord(args, rank, world, dev)
+            if not step_cfg and not args.no_step:
+                # configuration 4 (the 40-block step with 512 text tokens) as a sub-record: one block
+                # forward warms every kernel and shape of the step, then 2 timed steps, 1 step end to end
+                # through HostPipeline, and the final latent checked against the eager path
+                rs = dit_workload(args, rank, world, dev, 40, 252000, 512, 2, 0, trace=False,
+                                  e2e_steps=None if args.no_e2e else 1, serial=False,
+                                  parity=not args.no_parity, warm_blocks=1)
+                line["dit_step"] = {
+                    "metric": "DiT fwd ms/step (40-block step)", "value": round(rs["ms"], 1), "unit": "ms/step",
+                    "steps": 2, "warmup": "1 block forward (every kernel and shape of the step)",
+                    "config": dit_config(rs["cfg"], "dit_step", 252000, world, 40, 512, args.exchange),
+                    "clocks": rs["clocks"], "e2e": rs["e2e"], "parity": rs["parity"]}
         elif args.workload == "linear":
             ms, clocks, spans, launches = linear_workload(args, dev)
             M = args.rows or 4096
@@ -678,6 +862,19 @@ def main():
                     "config": {"workload": "linear", "M": M, "N": 5120, "K": 5120, "convrot_group": args.convrot,
                                "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
+                    "breakdown": breakdown(spans, pk)}
+        elif args.workload == "quant":
+            M, K, ms, clocks, spans, launches = quant_workload(args, dev)
+            gbs = (3 * M * K + 4 * M) / (ms * 1e-3) / 1e9
+            line = {"metric": f"{'GELU ' if args.act == 'gelu' else ''}activation quantiser GB/s", "value": round(gbs, 1),
+                    "unit": "GB/s", "ms_per_step": round(ms, 4), "n_gpus": 1, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16->int8",
+                    "config": {"workload": "quant", "M": M, "K": K, "act": args.act,
+                               "l2": "input larger than L2 (no flush)"},
+                    "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": round(gbs / pk["hbm_gbs"], 4), "traffic": None,
+                                 "peak_source": f"{pk_src} HBM copy bandwidth"},
+                    "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
         elif args.workload == "qkv_a2a":
             M, ms, clocks, spans, launches = qkv_a2a_workload(args, dev)

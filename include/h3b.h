@@ -180,8 +180,8 @@ H3B_API int h3b_int8_linear(const void *x, int64_t M, int64_t K, const int8_t *w
  * loads the library holds those 8.25 MiB until exit.  The first call on a
  * device looks up the arrays' device addresses (make it before any stream
  * capture).  Calls share the arrays: calls that overlap on the GPU race.
- * No counterpart in the reference (it always allocates x_q / x_s,
- * h3_linear_fast_patch.py:90-91); allocates nothing itself. */
+ * No counterpart in the reference, which always allocates its activation
+ * codes and scales; this entry point allocates nothing itself. */
 H3B_API int h3b_int8_linear_noalloc(const void *x, int64_t M, int64_t K, const int8_t *w, const float *ws,
                                     const void *bias, int64_t N, void *out, void *stream);
 

@@ -23,6 +23,7 @@
 // rows in L2.  Every mbarrier wait is bounded; on expiry the kernel records
 // H3B_STATUS_MBAR_TIMEOUT, stops issuing work, drains its own TMA loads and
 // MMAs (again bounded), frees TMEM and returns.
+#include <mutex>
 #include <cuda.h>
 #include <stdlib.h>
 
@@ -1087,22 +1088,33 @@ struct Scratch {
 
 // The host-side names g_codes / g_scales are stand-ins, not device addresses:
 // the device addresses are looked up once per device, with that device
-// current, on the first call made on it.
+// current, on the first call made on it.  The lookup runs under a per-device
+// std::call_once, so host threads making their first calls at the same time
+// all see both addresses or the lookup's error, never half a result.
+constexpr int kMaxDevices = 64;
+
+struct DeviceSlot {
+    std::once_flag once;
+    Scratch sc{nullptr, nullptr};
+    cudaError_t err = cudaSuccess;
+};
+
 static int scratch_for_current_device(Scratch* out) {
-    constexpr int kMaxDevices = 64;
-    static Scratch cache[kMaxDevices] = {};
+    static DeviceSlot slots[kMaxDevices];
     int dev = 0;
     H3B_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return set_error(H3B_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-    if (!cache[dev].codes) {
+    DeviceSlot& slot = slots[dev];
+    std::call_once(slot.once, [&slot] {
         void* c = nullptr;
         void* s = nullptr;
-        H3B_CUDA_TRY(cudaGetSymbolAddress(&c, g_codes));
-        H3B_CUDA_TRY(cudaGetSymbolAddress(&s, g_scales));
-        cache[dev].scales = static_cast<float*>(s);
-        cache[dev].codes = static_cast<int8_t*>(c);
-    }
-    *out = cache[dev];
+        cudaError_t e = cudaGetSymbolAddress(&c, g_codes);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&s, g_scales);
+        if (e == cudaSuccess) slot.sc = Scratch{static_cast<int8_t*>(c), static_cast<float*>(s)};
+        slot.err = e;
+    });
+    if (slot.err != cudaSuccess) return cuda_error(slot.err, "cudaGetSymbolAddress(noalloc scratch)");
+    *out = slot.sc;
     return H3B_OK;
 }
 
@@ -1119,6 +1131,12 @@ extern "C" int h3b_int8_linear_noalloc(const void* x, int64_t M, int64_t K, cons
     H3B_REQUIRE(M * K <= noalloc::kCodesBytes,
                 "h3b_int8_linear_noalloc: M*K=%lld exceeds the built-in %lld-byte activation buffer; use h3b_int8_linear",
                 (long long)(M * K), (long long)noalloc::kCodesBytes);
+    // every host-side check of the allocating path runs before the first CUDA
+    // call (the scratch lookup creates the context and loads the module)
+    H3B_REQUIRE(x && w && ws && out, "h3b_int8_linear_noalloc: NULL pointer");
+    H3B_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(out, 16) && aligned(ws, 16) && (!bias || aligned(bias, 16)),
+                "h3b_int8_linear_noalloc: x, w, ws, bias and out must be 16-byte aligned");
+    H3B_REQUIRE(N > 0 && N % 8 == 0, "h3b_int8_linear_noalloc: N=%lld must be a positive multiple of 8", (long long)N);
     noalloc::Scratch sc;
     if (int rc = noalloc::scratch_for_current_device(&sc)) return rc;
     return h3b_int8_linear(x, M, K, w, ws, bias, N, out, sc.codes, sc.scales, stream);

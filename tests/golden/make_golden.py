@@ -14,7 +14,7 @@ tl.math.rsqrt is 1/np.sqrt.  The oracle reproduces the fixtures exactly in the
 matching mode (oracle.TRUNC, fma=False, RSQRT_RECIP); the product mode differs
 only in those three switches.
 
-Also recorded: the modulation-table expression of h3_fuse_patch.py:305
+Also recorded: the modulation-table expression of h3_fuse_patch.py:113,116
 (`1.0 + scale.to(bf16)`) evaluated by PyTorch on CPU, which is the reference's
 own statement run as written.
 
@@ -91,7 +91,7 @@ def main(ref_root):
         scale = (0.1 * torch.randn(R, D, generator=g)).to(torch.bfloat16)
         shift = (0.1 * torch.randn(R, D, generator=g)).to(torch.bfloat16)
         gate = (0.1 * torch.randn(R, D, generator=g)).to(torch.bfloat16)
-        s1 = (1.0 + scale.to(torch.bfloat16)).contiguous()      # h3_fuse_patch.py:305
+        s1 = (1.0 + scale.to(torch.bfloat16)).contiguous()      # h3_fuse_patch.py:113,116
         ridx = torch.randint(0, R, (S,), generator=g, dtype=torch.int32)
         h_nm = fk.norm_mod(x, w, eps, ridx, s1, shift)
         x_g = x.clone()

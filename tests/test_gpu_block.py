@@ -83,3 +83,44 @@ def test_host_pipeline_matches_serial_steps():
 def test_block_with_qk_norm():
     """The block with the per-head q/k RMSNorm (rms_norm kernel on the unfused path)."""
     _run(hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816, qk_norm=True), S=1000, R=2, seed=6)
+
+
+def test_step_two_blocks_with_text_full_width():
+    """Configuration 4's structure at full width: two blocks of the step model
+    (D=5120, 40 heads, FFN 13824, 512 text tokens for the cross-attention), one
+    latent frame of rows, bit-exact against the eager block loop
+    (sp_forward.py:556-561 runs the blocks in order the same way)."""
+    cfg = hm.DiTConfig(n_blocks=2, text_len=512)
+    S = 4128
+    dit = hm.SynthDiT(cfg, DEV, seed=21)
+    x = randn_bf16((S, cfg.dim), 21).to(DEV)
+    text = randn_bf16((512, cfg.dim), 22).to(DEV)
+    ridx = torch.zeros(S, dtype=torch.int32, device=DEV)
+    y = dit.forward(x.clone(), ridx, None, text)
+    y_ref = x.clone()
+    for p in dit.params:
+        y_ref = tp.block_forward(cfg, p, y_ref, ridx, None, text)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all()
+    n_bad = (y.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
+    assert n_bad == 0, f"{n_bad} of {y.numel()} elements differ after 2 blocks"
+    assert h3b.status() == 0
+
+
+def test_block_full_size_s128000():
+    """Configuration 3 at its full size: one block over S=128000 tokens on one
+    GPU (the benchmark's block) against the eager block, bit for bit."""
+    cfg = hm.DiTConfig()
+    S = 128000
+    p = hm.make_params(cfg, 0, 1, DEV)
+    x = randn_bf16((S, cfg.dim), 31).to(DEV)
+    ridx = torch.zeros(S, dtype=torch.int32, device=DEV)
+    y = hm.block_forward(cfg, p, x.clone(), ridx)
+    y_ref = tp.block_forward(cfg, p, x, ridx)  # in place on x: the input is not needed again
+    torch.cuda.synchronize()
+    n_bad = (y.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
+    assert n_bad == 0, f"{n_bad} of {y.numel()} elements differ at S=128000"
+    assert torch.isfinite(y.float()).all()
+    assert h3b.status() == 0
+    del y, y_ref, x
+    torch.cuda.empty_cache()

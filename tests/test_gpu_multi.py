@@ -11,6 +11,11 @@ restatement locally.  Checked bit-exactly:
   * the same exchanges done the reference's way (reshape + all_to_all_single);
   * the exchange/attention overlap by head groups (both back ends, several
     group counts) against the plain exchange;
+  * configuration 2 at its full size (S=131072): forward + inverse exchange as
+    an identity round trip on both back ends, forward equal to the reference's
+    reshape + all_to_all_single;
+  * two blocks of the 40-block step model (512 text tokens) over an uneven
+    row split against the eager block loop;
   * one full DiT block (p2p exchange: fused into the qkv GEMM's epilogue and
     the out projection's quantiser, as separate kernels, and the overlap)
     against the eager PyTorch block using all_to_all_single.
@@ -100,6 +105,51 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize(dev)
             dist.barrier(device_ids=[rank])
             peer.close()
+        # configuration 2 at its full size: S=131072, q/k/v forward + inverse of the
+        # received q is an identity round trip, on both back ends (and equal to
+        # the reference's reshape + all_to_all_single formulation)
+        S = 131072
+        peer = h3b.PeerExchange(g, rank, world, S, H, Dh)
+        ctx_n = h3b.SPContext(rank, world, g, S)
+        mine = [torch.randn(ctx_n.local, H, Dh, generator=torch.Generator().manual_seed(1000 * i + rank))
+                .to(torch.bfloat16).to(dev) for i in range(3)]
+        ref_q = tp.a2a_gather_seq_scatter_heads(mine[0], ctx_n)
+        for exch in ("nccl", "p2p"):
+            ctx = h3b.SPContext(rank, world, g, S, exchange=exch, peer=peer if exch == "p2p" else None)
+            for rep in range(2):
+                qq, kk, vv = h3b.a2a_gather_qkv(*mine, ctx)
+                assert torch.equal(qq.view(torch.int16), ref_q.view(torch.int16)), f"{exch} fwd at S={S}"
+                back = h3b.a2a_scatter_seq_gather_heads(qq.reshape(S, -1), ctx)
+                assert torch.equal(back.reshape(-1).view(torch.int16), mine[0].reshape(-1).view(torch.int16)), \
+                    f"{exch} round trip at S={S}"
+                back_v = h3b.a2a_scatter_seq_gather_heads(vv.reshape(S, -1), ctx)
+                assert torch.equal(back_v.reshape(-1).view(torch.int16), mine[2].reshape(-1).view(torch.int16)), \
+                    f"{exch} v round trip at S={S}"
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[rank])
+        peer.close()
+        del mine, ref_q
+        # two blocks of the 40-block step model (512 text tokens, cross-attention)
+        # over an uneven row split, p2p exchange, against the eager block loop
+        cfg_s = hm.DiTConfig(n_blocks=2, text_len=512)
+        S = 4128 + world - 1
+        dit = hm.SynthDiT(cfg_s, dev, seed=23)
+        full = torch.randn(S, cfg_s.dim, generator=torch.Generator().manual_seed(24)).to(torch.bfloat16)
+        text = torch.randn(512, cfg_s.dim, generator=torch.Generator().manual_seed(25)).to(torch.bfloat16).to(dev)
+        peer = h3b.PeerExchange(g, rank, world, S, cfg_s.heads, cfg_s.head_dim)
+        ctx = h3b.SPContext(rank, world, g, S, exchange="p2p", peer=peer)
+        x = full[ctx.start:ctx.stop].to(dev)
+        ridx = torch.zeros(ctx.local, dtype=torch.int32, device=dev)
+        y = dit.forward(x.clone(), ridx, ctx, text)
+        y_ref = x.clone()
+        for p in dit.params:
+            y_ref = tp.block_forward(cfg_s, p, y_ref, ridx, h3b.SPContext(rank, world, g, S), text)
+        torch.cuda.synchronize(dev)
+        bad = (y.view(torch.int16) != y_ref.view(torch.int16)).sum().item()
+        assert bad == 0, f"2-block step with text at world {world}: {bad} elements differ"
+        dist.barrier(device_ids=[rank])
+        peer.close()
+        del dit
         # one full block at this world size against the eager block
         cfg = hm.DiTConfig()
         S = 4128

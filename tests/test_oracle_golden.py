@@ -34,7 +34,7 @@ def test_norm_kernels_match_reference_kernels(name):
     d = load(name)
     mode = dict(fma=False, rsqrt_mode=oracle.RSQRT_RECIP, final_round=oracle.TRUNC)
     eps = float(d["eps"])
-    # s1 = bf16(1.0 + scale): the reference evaluates it with PyTorch (RNE), h3_fuse_patch.py:305
+    # s1 = bf16(1.0 + scale): the reference evaluates it with PyTorch (RNE), h3_fuse_patch.py:113,116
     np.testing.assert_array_equal(oracle.one_plus(d["scale"], oracle.RNE), d["s1"])
     h, _ = oracle.norm_mod(d["x"], d["w"], eps, d["ridx"], d["s1"], d["shift"], **mode)
     np.testing.assert_array_equal(h, d["h_norm_mod"])

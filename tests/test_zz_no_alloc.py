@@ -27,21 +27,22 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def _inputs(M, K, N, seed):
+def _inputs(M, K, N, seed, dev=DEV):
     g = torch.Generator().manual_seed(seed)
-    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
-    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(DEV)
-    ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(DEV)
-    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(dev)
+    ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(dev)
+    b = (torch.randn(N, generator=g) * 0.02).to(torch.bfloat16).to(dev)
     return x, w, ws, b
 
 
 def _allocating(x, w, ws, b, stream):
     M, K = x.shape
     N = w.shape[0]
-    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
-    xq = torch.empty(M, K, dtype=torch.int8, device=DEV)
-    xs = torch.empty(M, dtype=torch.float32, device=DEV)
+    dev = x.device
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    xq = torch.empty(M, K, dtype=torch.int8, device=dev)
+    xs = torch.empty(M, dtype=torch.float32, device=dev)
     rc = lib.h3b_int8_linear(_p(x), M, K, _p(w), _p(ws), _p(b), N, _p(out), _p(xq), _p(xs), stream)
     assert rc == H3B_OK, lib.h3b_last_error()
     return out
@@ -50,7 +51,7 @@ def _allocating(x, w, ws, b, stream):
 def _noalloc(x, w, ws, b, stream):
     M, K = x.shape
     N = w.shape[0]
-    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     rc = lib.h3b_int8_linear_noalloc(_p(x), M, K, _p(w), _p(ws), _p(b), N, _p(out), stream)
     assert rc == H3B_OK, lib.h3b_last_error()
     return out
@@ -69,6 +70,32 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls():
         got = _noalloc(x, w, ws, b, stream)
         torch.cuda.synchronize(DEV)
         assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), f"mismatch at M={M} K={K} N={N}"
+    assert h3b.status() == 0
+
+
+def test_noalloc_on_a_second_device():
+    """Each GPU has its own copy of the built-in arrays, looked up with that GPU
+    current: after calls on device 0, calls on device 1 (two in a row) still
+    equal the allocating entry point there."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    x0, w0, ws0, b0 = _inputs(512, 1024, 256, 5)
+    s0 = ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    with torch.cuda.device(DEV):
+        first = _noalloc(x0, w0, ws0, b0, s0)
+    dev1 = torch.device("cuda", 1)
+    with torch.cuda.device(dev1):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev1).cuda_stream)
+        for (M, K, N, seed) in [(1000, 2048, 512, 3), (64, 5120, 1024, 4)]:
+            x, w, ws, b = _inputs(M, K, N, seed, dev1)
+            ref = _allocating(x, w, ws, b, stream)
+            got = _noalloc(x, w, ws, b, stream)
+            torch.cuda.synchronize(dev1)
+            assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), f"device 1 mismatch at M={M}"
+    with torch.cuda.device(DEV):
+        again = _noalloc(x0, w0, ws0, b0, s0)
+        torch.cuda.synchronize(DEV)
+    assert torch.equal(first.view(torch.int16), again.view(torch.int16))
     assert h3b.status() == 0
 
 
