@@ -62,7 +62,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a", "quant"],
+    ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a", "quant",
+                                           "vs_triton", "nvlink_probe"],
                     default="dit_block")
     ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
     ap.add_argument("--qknorm", action="store_true", help="qkv_a2a workload: with the per-head q/k RMSNorm")
@@ -329,7 +330,7 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup,
 
         # pipelined: HostPipeline, input copy of step k+1 / output copy of step
         # k-1 on copy streams during step k (three device slots)
-        pipe = hm.HostPipeline(dit, s_local, ridx, ctx, text, depth=3)
+        pipe = hm.HostPipeline(dit, s_local, ridx, ctx, text, depth=3, timing=True)
         outs = [torch.empty_like(x_host).pin_memory() for _ in range(3)]
 
         def step_pipe():
@@ -337,6 +338,7 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup,
 
         ms_e2e, _ = timed(step_pipe, e2e_steps, 1 if serial else 0, world, dev, sample_clocks=False,
                           finish=pipe.flush)
+        ct = pipe.copy_times()
         del pipe
         out_host = outs[0]
         h2d = x_host.numel() * 2 + sum(e.numel() * 2 for e in e_host)
@@ -344,6 +346,11 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup,
                "d2h_bytes_per_step": out_host.numel() * 2,
                "api": "h3b.model.HostPipeline.submit (pinned host latents in and out; copies on two copy streams "
                       "overlap the neighbouring steps' compute, every step's copies inside the timed region)"}
+        if ct["in"] and ct["out"]:
+            # each rank's own copies (CUDA events on the copy streams), warm-up step included
+            e2e["copy_in_ms"], e2e["copy_out_ms"] = round(ct["in"], 3), round(ct["out"], 3)
+            e2e["copy_in_gbs"] = round(x_host.numel() * 2 / ct["in"] / 1e6, 1)
+            e2e["copy_out_gbs"] = round(x_host.numel() * 2 / ct["out"] / 1e6, 1)
         if serial:
             # serial: copy in, forward, copy out, all on the compute stream
             def step_serial():
@@ -706,6 +713,192 @@ def a2a_workload(args, rank, world, dev):
     return S, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
 
 
+def nvlink_probe_workload(args):
+    """One process, two GPUs (no rank waits on another): rank 0's side of a
+    2-rank forward exchange.  On GPU 0 the forward-exchange copy kernel
+    (h3b_a2a_fwd_p2p, q/k/v [s_local, 40, 128]) and the qkv GEMM with the
+    exchange in its epilogue (h3b_int8_mm_scaled_a2a) store half of their
+    output into receive buffers on GPU 1 (peer access enabled) with plain
+    stores, the other half locally; the host synchronises between launches.
+    For ncu's NVLink byte counters next to CUDA-event timings; the payload that
+    crosses NVLink is s_local x 3 x 2560 x 2 bytes per launch."""
+    import ctypes
+
+    import h3b
+    from cuda.bindings import runtime as rt
+    from h3b._lib import check, lib, ptr_array, stream_of
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("the nvlink_probe workload needs 2 GPUs in one process")
+    for a, b in ((0, 1), (1, 0)):
+        torch.cuda.set_device(a)
+        (err,) = rt.cudaSetDevice(a)
+        (err,) = rt.cudaDeviceEnablePeerAccess(b, 0)
+        if err not in (rt.cudaError_t.cudaSuccess, rt.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+            raise SystemExit(f"cudaDeviceEnablePeerAccess({a}->{b}) failed: {err}")
+    d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+    torch.cuda.set_device(d0)
+    P, H, Dh = 2, 40, 128
+    s_local = args.rows or 16384
+    S, chunk = P * s_local, H // P * Dh
+    src = [seeded_rows(0, s_local, H * Dh, seed=40 + i).to(d0) for i in range(3)]
+    recv = [[torch.zeros(S, chunk, dtype=torch.bfloat16, device=d) for d in (d0, d1)] for _ in range(3)]
+    dst = [recv[i][j].data_ptr() for i in range(3) for j in range(P)]
+    off = s_local * chunk * 2 * 3  # bytes per launch that cross NVLink (the half for rank 1)
+    src_arr, k1 = ptr_array([t.data_ptr() for t in src])
+    dst_arr, k2 = ptr_array(dst)
+
+    def copy():
+        check(lib.h3b_a2a_fwd_p2p(3, src_arr, H * Dh * 2, dst_arr, s_local, 0, chunk * 2, chunk * 2, 0, P,
+                                  stream_of(src[0])), "h3b_a2a_fwd_p2p")
+    g = torch.Generator().manual_seed(0)
+    xq = torch.randint(-127, 128, (s_local, H * Dh), generator=g, dtype=torch.int8).to(d0)
+    xs = (torch.rand(s_local, 1, generator=g) * 0.05 + 1e-3).to(d0)
+    w = torch.randint(-127, 128, (3 * H * Dh, H * Dh), generator=g, dtype=torch.int8).to(d0)
+    ws = (torch.rand(3 * H * Dh, generator=g) * 9e-3 + 1e-3).to(d0)
+    bias = (torch.randn(3 * H * Dh, generator=g) * 0.02).to(torch.bfloat16).to(d0)
+
+    def gemm():
+        h3b.int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst, 0, H * Dh, Dh, H // P, P)
+    res = {}
+    for name, fn in (("a2a_fwd_p2p", copy), ("gemm_i8_scatter_qkv", gemm)):
+        ms = _event_time(lambda: (fn(), torch.cuda.synchronize(d1)), args.steps, warmup=args.warmup)
+        res[name] = {"ms": round(ms, 4), "nvlink_payload_bytes": off,
+                     "nvlink_payload_gbs": round(off / ms / 1e6, 1)}
+    # the rows rank 1 received equal rank 0's own pack of its heads 20..39
+    ok = all(torch.equal(recv[i][1][:s_local].view(torch.int16),
+                         src[i].view(s_local, P, chunk)[:, 1].contiguous().to(d1).view(torch.int16)) for i in range(3))
+    del k1, k2
+    return s_local, res, ok
+
+
+def load_reference_triton():
+    """The reference's own Triton kernel modules (int8_gemm_triton.py,
+    h3_fuse_kernels.py), unmodified, from baseline/_ref/comfyui_nodes (the
+    reference has no installable package for them; they are copied there as
+    its install, git-ignored).  Returns {"gemm": module, "fuse": module} or
+    None when they are absent (e.g. a checkout without the reference)."""
+    import importlib.util
+    base = os.path.join(ROOT, "baseline", "_ref", "comfyui_nodes")
+    mods = {}
+    for key, rel in (("gemm", os.path.join("h3-linear-fast", "int8_gemm_triton.py")),
+                     ("fuse", os.path.join("h3-fuse-graph", "h3_fuse_kernels.py"))):
+        path = os.path.join(base, rel)
+        if not os.path.exists(path):
+            return None
+        spec = importlib.util.spec_from_file_location(f"h3ref_{key}", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mods[key] = mod
+    return mods
+
+
+def _event_time(fn, iters, flush=None, warmup=3):
+    """Mean ms of fn() over iters launches, each timed alone with CUDA events on
+    the current stream (a flush of L2 before each, outside the events)."""
+    for _ in range(warmup):
+        fn()
+    total = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / iters
+
+
+def vs_triton_workload(args, dev, pk, pk_src):
+    """Same-box comparison: the reference's Triton INT8 GEMM and fused norm
+    kernels, this library's kernels and cuBLASLt (torch._int_mm + the eager
+    epilogue) on identical seeded inputs on one B200, each launch timed alone
+    with CUDA events after a 256 MB L2 flush; outputs compared bit for bit."""
+    import h3b
+    ref = load_reference_triton()
+    if ref is None:
+        return {"unavailable": "the reference's Triton modules are not under baseline/_ref/comfyui_nodes"}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    it = args.steps
+    out = {"gemm": [], "fused": [], "int_mm_peak": None}
+    shapes = [("config0", 4096, 5120, 5120), ("m32768", 32768, 5120, 5120),
+              ("block_qkv", 128000, 15360, 5120), ("block_out", 128000, 5120, 5120),
+              ("block_up", 128000, 13824, 5120), ("block_down", 128000, 5120, 13824)]
+    for name, M, N, K in shapes:
+        g = torch.Generator().manual_seed(M + N + K)
+        xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(dev)
+        w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(dev)
+        xs = (torch.rand(M, 1, generator=g) * 0.05 + 1e-3).to(dev)
+        ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(dev)
+        y_ref = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        y_ours = torch.empty_like(y_ref)
+        t_ref = _event_time(lambda: ref["gemm"].int8_mm_scaled(xq, w, xs, ws, out=y_ref), it, flush)
+        t_ours = _event_time(lambda: h3b.int8_mm_scaled(xq, w, xs, ws, out=y_ours), it, flush)
+
+        def cublas():
+            return ((torch._int_mm(xq, w.t()).float() * xs) * ws).to(torch.bfloat16)
+        t_cub = _event_time(cublas, max(2, it // 2), flush, warmup=1)
+        t_cub_mm = _event_time(lambda: torch._int_mm(xq, w.t()), it, flush)
+        y_cub = cublas()
+        torch.cuda.synchronize()
+        ops = 2.0 * M * N * K
+        rec = {"shape": name, "M": M, "N": N, "K": K,
+               "ms": {"reference_triton": round(t_ref, 4), "h3b": round(t_ours, 4),
+                      "cublaslt_int_mm_plus_eager_epilogue": round(t_cub, 4), "cublaslt_int_mm_only": round(t_cub_mm, 4)},
+               "tops": {"reference_triton": round(ops / t_ref / 1e9, 1), "h3b": round(ops / t_ours / 1e9, 1),
+                        "cublaslt_int_mm_only": round(ops / t_cub_mm / 1e9, 1)},
+               "speedup_vs_reference_triton": round(t_ref / t_ours, 3),
+               "speedup_vs_cublaslt_path": round(t_cub / t_ours, 3),
+               "bitexact_vs_reference_triton": bool(torch.equal(y_ref.view(torch.int16), y_ours.view(torch.int16))),
+               "bitexact_vs_cublaslt_path": bool(torch.equal(y_cub.view(torch.int16), y_ours.view(torch.int16)))}
+        out["gemm"].append(rec)
+        log(json.dumps(rec))
+        del xq, w, xs, ws, y_ref, y_ours, y_cub
+        torch.cuda.empty_cache()
+    # a measured INT8 rate of the box's own library GEMM (cuBLASLt int8 -> int32), beside the 2 x bf16 peak
+    n = 8192
+    g = torch.Generator().manual_seed(1)
+    a = torch.randint(-127, 128, (n, n), generator=g, dtype=torch.int8).to(dev)
+    b = torch.randint(-127, 128, (n, n), generator=g, dtype=torch.int8).to(dev)
+    t = _event_time(lambda: torch._int_mm(a, b.t()), it)
+    out["int_mm_peak"] = {"shape": f"{n}^3 int8 -> int32 (torch._int_mm, cuBLASLt)", "tops": round(2.0 * n ** 3 / t / 1e9, 1),
+                          "ms": round(t, 4), "vs_2x_bf16_burst": round(2.0 * n ** 3 / t / 1e9 / (2 * pk["bf16_tflops"]), 3)}
+    del a, b
+    # fused adaLN chain at configuration 1 (S=32768, D=5120, one modulation row)
+    S, D = args.rows or 32768, 5120
+    g = torch.Generator().manual_seed(6)
+    x0 = seeded_rows(0, S, D, seed=3).to(dev)
+    o1 = seeded_rows(0, S, D, seed=4).to(dev)
+    e = (0.1 * torch.randn(1, 6, D, generator=g)).to(torch.bfloat16).to(dev)
+    wn = (1 + 0.02 * torch.randn(D, generator=g)).to(torch.bfloat16).to(dev)
+    s1, sh, gt = h3b.modulation_tables(*(e[:, i] for i in range(6)))[:3]
+    ridx = torch.zeros(S, dtype=torch.int32, device=dev)
+    xa, xb = x0.clone(), x0.clone()
+    cases = [("norm_mod", 4 * S * D, lambda: ref["fuse"].norm_mod(xa, wn, 1e-6, ridx, s1, sh),
+              lambda: h3b.norm_mod(xb, wn, 1e-6, ridx, s1, sh)),
+             ("gate_norm_mod_", 8 * S * D, lambda: ref["fuse"].gate_norm_mod_(xa, o1, gt, wn, 1e-6, ridx, s1, sh),
+              lambda: h3b.gate_norm_mod_(xb, o1, gt, wn, 1e-6, ridx, s1, sh)),
+             ("gate_", 6 * S * D, lambda: ref["fuse"].gate_(xa, o1, gt, ridx), lambda: h3b.gate_(xb, o1, gt, ridx))]
+    for name, nbytes, f_ref, f_ours in cases:
+        # bit-equality on one call from the same state, then timing (the in-place ops keep changing x alike)
+        xa.copy_(x0)
+        xb.copy_(x0)
+        h_ref, h_ours = f_ref(), f_ours()
+        torch.cuda.synchronize()
+        same = bool(torch.equal(h_ref.view(torch.int16), h_ours.view(torch.int16))) and \
+            bool(torch.equal(xa.view(torch.int16), xb.view(torch.int16)))
+        t_ref = _event_time(f_ref, it, flush)
+        t_ours = _event_time(f_ours, it, flush)
+        rec = {"kernel": name, "S": S, "D": D, "ms": {"reference_triton": round(t_ref, 4), "h3b": round(t_ours, 4)},
+               "hbm_frac_of_measured": {"reference_triton": round(nbytes / t_ref / 1e6 / pk["hbm_gbs"], 3),
+                                        "h3b": round(nbytes / t_ours / 1e6 / pk["hbm_gbs"], 3)},
+               "speedup_vs_reference_triton": round(t_ref / t_ours, 3), "bitexact_vs_reference_triton": same}
+        out["fused"].append(rec)
+        log(json.dumps(rec))
+    return out
+
+
 def nvlink_counters(dev):
     """Cumulative NVLink bytes of this GPU from NVML (read-only counters), summed
     over its links: {"tx": bytes, "rx": bytes, "field": name} or None.  Tries the
@@ -863,6 +1056,19 @@ def main():
                                "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
+        elif args.workload == "nvlink_probe":
+            s_local, res, ok = nvlink_probe_workload(args)
+            line = {"metric": "forward exchange over NVLink, one process driving 2 GPUs (GB/s of payload)",
+                    "n_gpus": 2, "steps": args.steps, "warmup": args.warmup,
+                    "config": {"workload": "nvlink_probe", "s_local": s_local, "heads": 40, "head_dim": 128,
+                               "world": 2, "link_peak_gbs": 900.0},
+                    "payload_bitexact": ok, **res}
+        elif args.workload == "vs_triton":
+            res = vs_triton_workload(args, dev, pk, pk_src)
+            line = {"metric": "same-box comparison with the reference's Triton kernels", "n_gpus": 1,
+                    "steps": args.steps, "config": {"workload": "vs_triton", "l2": "256 MB flush before each launch"},
+                    "peak_source": f"{pk_src} (MEASURED_PEAKS.json: HBM {pk['hbm_gbs']} GB/s, bf16 {pk['bf16_tflops']} "
+                                   "TFLOP/s burst)", **res}
         elif args.workload == "quant":
             M, K, ms, clocks, spans, launches = quant_workload(args, dev)
             gbs = (3 * M * K + 4 * M) / (ms * 1e-3) / 1e9

@@ -101,8 +101,19 @@ H3B_API int h3b_swiglu_quant_convrot(const void *x, int64_t ldx, int64_t M, int6
  * -- the input of the FFN down projection -- without writing the activation.
  * Equals h3b_quant_rowwise(F.gelu(u, approximate="tanh")) bit for bit.  The
  * reference fuses its own activation (SwiGLU) into the quantiser the same way,
- * h3_linear_fast_patch.py:3-5,93-95 (input_act). */
+ * h3_linear_fast_patch.py:3-5,93-95 (input_act).  The GELU is read from a
+ * 65536-entry table (one bf16 output per bf16 input) that the first call on a
+ * device fills from that formula and waits for: make that first call before
+ * any stream capture.  It and h3b_gelu_tanh share the table. */
 H3B_API int h3b_gelu_quant(const void *u, int64_t ldu, int64_t M, int64_t K, int8_t *xq, float *xs, void *stream);
+
+/* y = F.gelu(x, approximate="tanh") on n bf16 elements (n even, x and y
+ * 16-byte aligned), bit for bit: the FFN activation between the up and down
+ * projections of the block's mlp (the self.mlp call of
+ * comfyui_nodes/h3-fuse-graph/h3_fuse_patch.py:133) when it is not fused into
+ * the down projection's quantiser.  Reads the table of h3b_gelu_quant (filled
+ * by the first call of either on a device). */
+H3B_API int h3b_gelu_tanh(const void *x, void *y, int64_t n, void *stream);
 
 /* INT8 GEMM with dequant epilogue on tcgen05 tensor cores:
  * acc[m,n] = sum_k xq[m,k] * w[n,k] (int32), out[m,n] =

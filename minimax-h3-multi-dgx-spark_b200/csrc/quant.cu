@@ -7,11 +7,14 @@
 // element is quantised with the reciprocal fast path of quant_common.cuh.
 // Bytes per row: 2K read, K + 4 written.
 //
-// GELU variant: each element first becomes bf16(gelu_tanh(x)) computed exactly
-// as PyTorch's GeluCUDAKernelImpl does in fp32 (x^3 as (x*x)*x, the inner
-// polynomial as one fused multiply-add, tanhf, 0.5*x*(1+t)), so the codes equal
-// quant(F.gelu(u, approximate="tanh")) bit for bit without the bf16 GELU output
-// ever reaching HBM.
+// GELU variant (h3b_gelu_quant, the input of the FFN down projection): the
+// codes of bf16(gelu_tanh(x)), the value PyTorch's GeluCUDAKernelImpl computes
+// in fp32 (x^3 as (x*x)*x, the inner polynomial as one fused multiply-add,
+// tanhf, 0.5*x*(1+t)), so they equal quant(F.gelu(u, approximate="tanh")) bit
+// for bit without the bf16 GELU output ever reaching HBM.  A bf16 input has
+// 65536 values, so the GELU is a 128 KB table filled once per device by that
+// formula; the kernel keeps it in shared memory and streams the rows past it
+// (gelu_quant_lut_kernel below).
 //
 // ConvRot variant (quant_convrot_kernel): the rows are first rotated group by
 // group with the Walsh-Hadamard transform, as the reference's fast path does
@@ -22,11 +25,15 @@
 // output rows, read over NVLink from the peers' buffers, so the exchanged rows
 // never land in a staging buffer; codes and scales are those of the gathered
 // row, bit for bit.
+#include <stdlib.h>
+
+#include <mutex>
+
 #include "quant_common.cuh"
 
 namespace h3b {
 
-enum class Act { kNone = 0, kGeluTanh = 1 };
+enum class Act { kNone = 0 };
 
 constexpr int kMaxGatherRanks = 8;
 
@@ -64,12 +71,6 @@ __global__ void __launch_bounds__(NT) quant_rowwise_kernel(const uint16_t* __res
     for (int i = 0; i < VPT; ++i) {
         const int j = threadIdx.x + i * NT;
         if (j < nvec) {
-            if constexpr (ACT == Act::kGeluTanh) {
-                v[i].x = gelu2(v[i].x);
-                v[i].y = gelu2(v[i].y);
-                v[i].z = gelu2(v[i].z);
-                v[i].w = gelu2(v[i].w);
-            }
             m = absmax_bits8(v[i], m);
         }
     }
@@ -203,6 +204,261 @@ __global__ void __launch_bounds__(NT) quant_convrot_kernel(const uint16_t* __res
     }
 }
 
+// Bounded mbarrier waits of the table-driven GELU kernels below.
+__device__ __forceinline__ bool bar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool bar_wait_parity_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+    if (bar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (bar_try_wait(bar, parity)) return true;
+        if ((n & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+__device__ __forceinline__ bool bar_wait_bounded(uint32_t bar, uint64_t limit_ns) {
+    if (bar_try_wait(bar, 0)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (bar_try_wait(bar, 0)) return true;
+        if ((n & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// GELU by table.  A bf16 -> bf16 function is determined by its 65536 outputs:
+// g_gelu_table[b] = gelu2 (PyTorch's fp32 formula with tanhf) of the bf16 with
+// bits b, filled once per device by gelu_table_fill_kernel from the exact
+// formula, so every lookup equals F.gelu(approximate="tanh") bit for bit.
+// The quantiser and the elementwise GELU keep the 128 KB table in shared
+// memory (one bulk copy per CTA), one persistent CTA of 1024 threads per SM.
+static __device__ __align__(128) uint16_t g_gelu_table[65536];
+constexpr int kTableBytes = 65536 * 2;
+constexpr int kLutThreads = 1024;
+constexpr int kLutSmemMax = 227 * 1024 - 1024;  // dynamic shared memory: the table and the row buffers
+
+__global__ void gelu_table_fill_kernel() {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;  // one bf16 pair per thread
+    if (i < 32768) {
+        const uint32_t v = gelu2((uint32_t)(2 * i) | ((uint32_t)(2 * i + 1) << 16));
+        reinterpret_cast<uint32_t*>(g_gelu_table)[i] = v;
+    }
+}
+
+// Bounded wait for the table's bulk copy (all threads); false on expiry.
+__device__ __forceinline__ bool load_table(uint16_t* lut, uint64_t* bar, int* status) {
+    const uint32_t sbar = (uint32_t)__cvta_generic_to_shared(bar);
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sbar) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sbar), "r"(kTableBytes) : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                (uint32_t)__cvta_generic_to_shared(lut)),
+            "l"(g_gelu_table), "r"(kTableBytes), "r"(sbar)
+            : "memory");
+    }
+    __syncthreads();
+    if (!bar_wait_bounded(sbar, 10ull * 1000 * 1000 * 1000)) {
+        report(status, H3B_STATUS_MBAR_TIMEOUT);
+        bar_wait_bounded(sbar, 100ull * 1000 * 1000);  // this CTA's own copy, before its shared memory goes
+        return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ uint32_t lut2(const uint16_t* lut, uint32_t v) {
+    return (uint32_t)lut[v & 0xFFFFu] | ((uint32_t)lut[v >> 16] << 16);
+}
+
+__device__ __forceinline__ uint4 lut8(const uint16_t* lut, uint4 v) {
+    return make_uint4(lut2(lut, v.x), lut2(lut, v.y), lut2(lut, v.z), lut2(lut, v.w));
+}
+
+// Rows r = blockIdx.x, + gridDim.x, ...: up to kMaxRowBufs rows ahead are in
+// flight as bulk copies into shared-memory row buffers (one mbarrier each),
+// so the bytes in flight per SM do not depend on registers.  Per row: wait
+// for its buffer, thread t takes vectors t, t + 1024, .. into registers,
+// looks them up, takes the absmax; one barrier per row (the per-warp maxima
+// alternate between two shared arrays) also frees the buffer, whose next row
+// thread 0 then requests; codes are written from the registers.
+constexpr int kMaxRowBufs = 3;
+
+template <int VPT>
+__global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const uint16_t* __restrict__ x, int64_t ldx,
+                                                                          int64_t M, int K, int8_t* __restrict__ xq,
+                                                                          float* __restrict__ xs, int nbuf,
+                                                                          int* status) {
+    extern __shared__ __align__(128) uint16_t lut[];  // 65536 table entries, then nbuf rows of K
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t full[kMaxRowBufs];
+    __shared__ uint32_t wmax[2][kLutThreads / 32];
+    const int nvec = K >> 3;
+    const int t = threadIdx.x;
+    const uint32_t row_bytes = (uint32_t)K * 2u;
+    uint4* rows = reinterpret_cast<uint4*>(lut + 65536);
+    const int64_t step = gridDim.x;
+    auto request = [&](int b, int64_t r) {  // thread 0 only
+        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sb), "r"(row_bytes) : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                (uint32_t)__cvta_generic_to_shared(rows + (int64_t)b * nvec)),
+            "l"(x + r * ldx), "r"(row_bytes), "r"(sb)
+            : "memory");
+    };
+    if (t == 0) {
+        for (int b = 0; b < nbuf; ++b)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&full[b]))
+                         : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int b = 0; b < nbuf; ++b)
+            if (blockIdx.x + b * step < M) request(b, blockIdx.x + b * step);
+    }
+    if (!load_table(lut, &bar, status)) {
+        if (t == 0)
+            for (int b = 0; b < nbuf; ++b)
+                if (blockIdx.x + b * step < M) bar_wait_bounded((uint32_t)__cvta_generic_to_shared(&full[b]),
+                                                                100ull * 1000 * 1000);
+        return;
+    }
+    int it = 0;
+    for (int64_t row = blockIdx.x; row < M; row += step, ++it) {
+        const int b = it % nbuf;
+        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
+        if (!bar_wait_parity_bounded(sb, (uint32_t)((it / nbuf) & 1), 10ull * 1000 * 1000 * 1000)) {
+            report(status, H3B_STATUS_MBAR_TIMEOUT);
+            if (t == 0)  // the copies this CTA still has in flight, before its shared memory goes
+                for (int k = 0; k < nbuf && row + k * step < M; ++k)
+                    bar_wait_parity_bounded((uint32_t)__cvta_generic_to_shared(&full[(it + k) % nbuf]),
+                                            (uint32_t)(((it + k) / nbuf) & 1), 100ull * 1000 * 1000);
+            return;
+        }
+        const uint4* rb = rows + (int64_t)b * nvec;
+        uint4 v[VPT];
+        uint32_t m = 0;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int j = t + i * kLutThreads;
+            if (j < nvec) {
+                v[i] = lut8(lut, rb[j]);
+                m = absmax_bits8(v[i], m);
+            }
+        }
+        uint32_t mb = max(m & 0xFFFFu, m >> 16);
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        if ((t & 31) == 0) wmax[it & 1][t >> 5] = mb;
+        __syncthreads();  // every thread has read buffer b: its next row may come in
+        if (t == 0 && row + nbuf * step < M) request(b, row + nbuf * step);
+        mb = __reduce_max_sync(0xffffffffu, wmax[it & 1][t & 31]);
+        float s, rc;
+        row_scale(__uint_as_float(mb << 16), s, rc);
+        if (t == 0) xs[row] = s;
+        uint2* qr = reinterpret_cast<uint2*>(xq + row * (int64_t)K);
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int j = t + i * kLutThreads;
+            if (j < nvec) {
+                float f[8];
+                unpack8(v[i], f);
+                qr[j] = quant8(f, s, rc);
+            }
+        }
+    }
+}
+
+// Elementwise bf16 GELU by table: grid-stride over 16-byte vectors.
+__global__ void __launch_bounds__(kLutThreads, 1) gelu_lut_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                                                                    int64_t nvec, const uint32_t* __restrict__ xt,
+                                                                    uint32_t* __restrict__ yt, int tail_pairs,
+                                                                    int* status) {
+    extern __shared__ __align__(128) uint16_t lut[];
+    __shared__ __align__(8) uint64_t bar;
+    const int64_t stride = (int64_t)gridDim.x * kLutThreads;
+    int64_t i = (int64_t)blockIdx.x * kLutThreads + threadIdx.x;
+    uint4 v = i < nvec ? x[i] : make_uint4(0u, 0u, 0u, 0u);
+    if (!load_table(lut, &bar, status)) return;
+    for (; i < nvec; i += stride) {
+        const uint4 nv = i + stride < nvec ? x[i + stride] : make_uint4(0u, 0u, 0u, 0u);
+        y[i] = lut8(lut, v);
+        v = nv;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < tail_pairs) yt[threadIdx.x] = lut2(lut, xt[threadIdx.x]);
+}
+
+// Per device, once: fill the table and allow the kernels their shared memory.
+// The first call on a device launches the fill kernel on the caller's stream
+// and waits for it (make that first call before any stream capture).
+static int gelu_table_ready(cudaStream_t s) {
+    struct Slot {
+        std::once_flag once;
+        cudaError_t err = cudaSuccess;
+    };
+    static Slot slots[64];
+    int dev = 0;
+    H3B_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(H3B_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    Slot& slot = slots[dev];
+    std::call_once(slot.once, [&slot, s] {
+        cudaError_t e = cudaFuncSetAttribute(gelu_quant_lut_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kLutSmemMax);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gelu_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTableBytes);
+        if (e == cudaSuccess) {
+            gelu_table_fill_kernel<<<128, 256, 0, s>>>();
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        slot.err = e;
+    });
+    if (slot.err != cudaSuccess) return cuda_error(slot.err, "GELU table set-up");
+    return H3B_OK;
+}
+
+static int num_sms_here() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+static int gelu_quant_lut(const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs, cudaStream_t s) {
+    if (int rc = gelu_table_ready(s)) return rc;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    const int nvec = K / 8;
+    const int vpt = (nvec + kLutThreads - 1) / kLutThreads;  // <= 4 for K <= 32768
+    const int row_bytes = K * 2;
+    int nbuf = (kLutSmemMax - kTableBytes) / row_bytes;  // >= 1 for K <= 32768
+    if (nbuf > kMaxRowBufs) nbuf = kMaxRowBufs;
+    const int smem = kTableBytes + nbuf * row_bytes;
+    const int64_t sms = num_sms_here();
+    const unsigned grid = (unsigned)(M < sms ? M : sms);
+    switch (vpt) {
+        case 1: gelu_quant_lut_kernel<1><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
+        case 2: gelu_quant_lut_kernel<2><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
+        case 3: gelu_quant_lut_kernel<3><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
+        default: gelu_quant_lut_kernel<4><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
+    }
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
+}
+
 template <int NT, int G, bool SWIGLU>
 static void launch_convrot(int vpt, const uint16_t* x, int64_t ldx, int64_t M, int K, int8_t* xq, float* xs,
                            cudaStream_t s) {
@@ -250,7 +506,11 @@ static int quant_impl(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* 
     H3B_REQUIRE(M < (1ll << 31), "%s: M too large", who);
     if (M == 0) return H3B_OK;
     const int nvec = (int)(K / 8);
+    // 128 threads per row up to 8 vectors each (K <= 8192); longer rows take 256
+    // threads (K = 13824: 0.92 vs 0.79 of the measured HBM bandwidth, fewer
+    // registers per thread and more rows resident)
     int vpt = pick_vpt((nvec + 127) / 128);
+    if (vpt > 8) vpt = -1;
     if (vpt > 0) {
         launch_quant<128, ACT>(vpt, static_cast<const uint16_t*>(x), ldx, M, (int)K, xq, xs, s);
     } else {
@@ -325,7 +585,38 @@ static int gather_quant(const void* const* src, int64_t src_ld, int64_t row_star
     return H3B_OK;
 }
 
+static int gelu_tanh(const void* x, void* y, int64_t n, cudaStream_t s) {
+    H3B_REQUIRE(x && y, "h3b_gelu_tanh: NULL pointer");
+    H3B_REQUIRE(n >= 0 && n % 2 == 0, "h3b_gelu_tanh: n=%lld must be even", (long long)n);
+    H3B_REQUIRE(aligned(x, 16) && aligned(y, 16), "h3b_gelu_tanh: x and y must be 16-byte aligned");
+    if (n == 0) return H3B_OK;
+    const int64_t nvec = n / 8;
+    const int tail_pairs = (int)((n % 8) / 2);
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = cdiv(nvec, 256);
+    const int grid = (int)(want < 1 ? 1 : (want < (int64_t)sms * 8 ? want : (int64_t)sms * 8));
+    const uint16_t* xb = static_cast<const uint16_t*>(x);
+    uint16_t* yb = static_cast<uint16_t*>(y);
+    if (int rc = gelu_table_ready(s)) return rc;
+    DeviceStatus ds;
+    if (int rc = device_status(&ds)) return rc;
+    const int64_t lut_want = cdiv(nvec, kLutThreads);
+    const unsigned lut_grid = (unsigned)(lut_want < 1 ? 1 : (lut_want < sms ? lut_want : sms));
+    gelu_lut_kernel<<<lut_grid, kLutThreads, kTableBytes, s>>>(
+        reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(y), nvec,
+        reinterpret_cast<const uint32_t*>(xb + nvec * 8), reinterpret_cast<uint32_t*>(yb + nvec * 8), tail_pairs,
+        ds.word);
+    H3B_CUDA_TRY(cudaGetLastError());
+    return H3B_OK;
+}
+
 }  // namespace h3b
+
+extern "C" int h3b_gelu_tanh(const void* x, void* y, int64_t n, void* stream) {
+    return h3b::gelu_tanh(x, y, n, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int h3b_quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t K, int8_t* xq, float* xs,
                                  void* stream) {
@@ -334,8 +625,16 @@ extern "C" int h3b_quant_rowwise(const void* x, int64_t ldx, int64_t M, int64_t 
 
 extern "C" int h3b_gelu_quant(const void* u, int64_t ldu, int64_t M, int64_t K, int8_t* xq, float* xs,
                               void* stream) {
-    return h3b::quant_impl<h3b::Act::kGeluTanh>(u, ldu, M, K, xq, xs, static_cast<cudaStream_t>(stream),
-                                                "h3b_gelu_quant");
+    using namespace h3b;
+    const char* who = "h3b_gelu_quant";
+    H3B_REQUIRE(u && xq && xs, "%s: NULL pointer", who);
+    H3B_REQUIRE(M >= 0 && M < (1ll << 31) && K > 0 && K % 8 == 0 && K <= 32768,
+                "%s: K=%lld must be a positive multiple of 8 <= 32768", who, (long long)K);
+    H3B_REQUIRE(ldu >= K && ldu % 8 == 0 && aligned(u, 16),
+                "%s: u must be 16-byte aligned with ldu %% 8 == 0 (ldu=%lld)", who, (long long)ldu);
+    H3B_REQUIRE(aligned(xq, 8), "%s: xq must be 8-byte aligned", who);
+    if (M == 0) return H3B_OK;
+    return gelu_quant_lut(static_cast<const uint16_t*>(u), ldu, M, (int)K, xq, xs, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int h3b_a2a_inv_quant(const void* const* src, int64_t src_ld, int64_t row_start, int64_t M,

@@ -13,13 +13,13 @@ benchmark and HostPipeline, the host-latent runner.
 from ._lib import H3BError, clear_status, lib, status  # noqa: F401
 from .fuse import (gate_, gate_norm_mod_, gate_norm_mod_quant_, modulation_tables, norm_mod,  # noqa: F401
                    norm_mod_quant, rms_norm, row_index)
-from .linear import (gelu_quant, int8_linear, int8_mm_i32, int8_mm_scaled, int8_mm_scaled_a2a, linear,  # noqa: F401
+from .linear import (gelu_quant, gelu_tanh, int8_linear, int8_mm_i32, int8_mm_scaled, int8_mm_scaled_a2a, linear,  # noqa: F401
                      quant_rowwise, quant_rowwise_convrot, supported, swiglu_quant_convrot)
 from .sp import (PeerExchange, SPContext, a2a_gather_qkv, a2a_gather_seq_scatter_heads,  # noqa: F401
                  a2a_scatter_seq_gather_heads, gather_rows, overlap_groups, pack, sp_attention_overlap, startup_probe, unpack)
 
 __all__ = ["H3BError", "status", "clear_status", "norm_mod", "rms_norm", "gate_norm_mod_", "gate_", "row_index",
-           "norm_mod_quant", "gate_norm_mod_quant_", "gelu_quant",
+           "norm_mod_quant", "gate_norm_mod_quant_", "gelu_quant", "gelu_tanh",
            "modulation_tables", "quant_rowwise", "quant_rowwise_convrot", "swiglu_quant_convrot", "int8_mm_scaled", "int8_mm_scaled_a2a", "int8_mm_i32", "int8_linear",
            "linear",
            "supported", "SPContext", "PeerExchange", "a2a_gather_seq_scatter_heads", "a2a_scatter_seq_gather_heads",

@@ -42,6 +42,7 @@ SIGNATURES = [
     ("h3b_norm_mod_quant", _I32, [_P, _P, _F32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_gate_norm_mod_quant_", _I32, [_P, _P, _P, _P, _F32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("h3b_gelu_quant", _I32, [_P, _I64, _I64, _I64, _P, _P, _P]),
+    ("h3b_gelu_tanh", _I32, [_P, _P, _I64, _P]),
     ("h3b_a2a_pack", _I32, [_P, _I64, _P, _I64, _I64, _I64, _I32, _P]),
     ("h3b_a2a_unpack", _I32, [_P, _P, _I64, _I64, _I64, _I64, _I32, _P]),
     ("h3b_ipc_handle", _I32, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),

@@ -90,6 +90,18 @@ def gelu_quant(u, xq=None, xs=None):
     return xq, xs
 
 
+def gelu_tanh(u, out=None):
+    """F.gelu(u, approximate="tanh") for bf16 u (any shape, contiguous), bit for bit."""
+    require_cuda(u)
+    if u.dtype != torch.bfloat16 or not u.is_contiguous() or u.numel() % 2:
+        raise ValueError("gelu_tanh: u must be a contiguous bf16 tensor with an even number of elements")
+    if out is None:
+        out = torch.empty_like(u)
+    with span("gelu", 4 * u.numel()):
+        check(lib.h3b_gelu_tanh(ptr(u), ptr(out), u.numel(), stream_of(u)), "h3b_gelu_tanh")
+    return out
+
+
 def _gemm_checks(xq, w):
     require_cuda(xq, w)
     if xq.dtype != torch.int8 or w.dtype != torch.int8 or xq.dim() != 2 or w.dim() != 2:

@@ -38,6 +38,7 @@ import torch.nn.functional as F
 
 from . import fuse, sp
 from .linear import gelu_quant as _gelu_quant
+from .linear import gelu_tanh as _gelu
 from .linear import int8_mm_scaled as _mm8
 from .linear import linear as _linear8
 from .linear import quant_rowwise as _quant
@@ -232,7 +233,7 @@ def block_forward(cfg, p, x, ridx, ctx=None, text=None, fused_producers=None, ov
     else:
         u = _lin_q(hq, p.up)
         del hq
-        aq = _gelu_quant(u) if fused_gelu else _quant(F.gelu(u, approximate="tanh"))
+        aq = _gelu_quant(u) if fused_gelu else _quant(_gelu(u))
         del u
     m = _lin_q(aq, p.down)
     del aq
@@ -267,9 +268,11 @@ class HostPipeline:
     copy issued so far: out_host of a submitted step is valid once the current
     stream has passed that point (e.g. after flush() and a synchronize).
     `before` (optional) is called on the current stream before each forward,
-    for per-step device inputs such as the modulation tables."""
+    for per-step device inputs such as the modulation tables.  With
+    timing=True the copies are bracketed by CUDA events on their streams and
+    copy_times() returns their mean durations."""
 
-    def __init__(self, model, rows, ridx, ctx=None, text=None, depth=3):
+    def __init__(self, model, rows, ridx, ctx=None, text=None, depth=3, timing=False):
         self.model, self.ridx, self.ctx, self.text = model, ridx, ctx, text
         dev = model.device
         self.device = dev
@@ -278,6 +281,23 @@ class HostPipeline:
         self.copy_in = torch.cuda.Stream(device=dev)
         self.copy_out = torch.cuda.Stream(device=dev)
         self.k = 0
+        self.timing = timing
+        self._ev = {"in": [], "out": []}
+
+    def _timed_copy(self, kind, stream, dst, src):
+        if not self.timing:
+            dst.copy_(src, non_blocking=True)
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dst.copy_(src, non_blocking=True)
+        e1.record(stream)
+        self._ev[kind].append((e0, e1))
+
+    def copy_times(self):
+        """{"in": mean ms, "out": mean ms} of the timed copies so far (synchronises)."""
+        torch.cuda.synchronize(self.device)
+        return {k: (sum(a.elapsed_time(b) for a, b in v) / len(v) if v else None) for k, v in self._ev.items()}
 
     def submit(self, x_host, out_host, before=None):
         i = self.k % len(self.slots)
@@ -286,7 +306,7 @@ class HostPipeline:
         with torch.cuda.stream(self.copy_in):
             if self.freed[i] is not None:
                 self.copy_in.wait_event(self.freed[i])
-            slot.copy_(x_host, non_blocking=True)
+            self._timed_copy("in", self.copy_in, slot, x_host)
             ready = torch.cuda.Event()
             ready.record(self.copy_in)
         cur.wait_event(ready)
@@ -297,7 +317,7 @@ class HostPipeline:
         done.record(cur)
         self.copy_out.wait_event(done)
         with torch.cuda.stream(self.copy_out):
-            out_host.copy_(y, non_blocking=True)
+            self._timed_copy("out", self.copy_out, out_host, y)
             freed = torch.cuda.Event()
             freed.record(self.copy_out)
         self.freed[i] = freed

@@ -79,6 +79,40 @@ def _seq_scatter(out, send, ctx, width, async_op=False):
                                   group=ctx.group, async_op=async_op)
 
 
+def _seq_gather_group(outs, sends, ctx, width):
+    """_seq_gather of several tensors as ONE group of point-to-point transfers
+    (torch.distributed.batch_isend_irecv: one ncclGroupStart/End on NCCL): for
+    each tensor, this rank's chunk for rank j goes to j and rank j's rows land
+    at their place in the output; the own chunk is a local copy.  sends[i] is
+    [P * local * width] in destination order (the pack layout), outs[i] is
+    [S * width].  Returns the requests to wait on."""
+    ops = []
+    starts = [0]
+    for n in ctx.splits:
+        starts.append(starts[-1] + n)
+    me = ctx.rank
+    for out, send in zip(outs, sends):
+        src = send.view(ctx.world, ctx.local * width)
+        for j in range(ctx.world):
+            if j == me:
+                continue
+            ops.append(dist.P2POp(dist.isend, src[j], _global_rank(ctx, j), group=ctx.group))
+            ops.append(dist.P2POp(dist.irecv, out[starts[j] * width: starts[j + 1] * width], _global_rank(ctx, j),
+                                  group=ctx.group))
+    reqs = dist.batch_isend_irecv(ops) if ops else []
+    for out, send in zip(outs, sends):
+        out[starts[me] * width: starts[me + 1] * width].copy_(send.view(ctx.world, -1)[me])
+    return reqs
+
+
+def _global_rank(ctx, j):
+    """Global rank of group rank j (P2P ops name peers by global rank)."""
+    g = ctx.group
+    if g is None or g == dist.group.WORLD:
+        return j
+    return dist.get_global_rank(g, j)
+
+
 def _rows(t):
     """View t as [rows, row_elems] with unit element stride inside a row; returns (t2d, row stride)."""
     t2 = t.reshape(t.shape[0], -1) if t.dim() != 2 else t
@@ -146,21 +180,20 @@ def a2a_gather_seq_scatter_heads(t, ctx):
 
 
 def a2a_gather_qkv(q, k, v, ctx):
-    """The three forward exchanges of one attention call at once (one launch /
-    one NCCL group instead of three)."""
+    """The three forward exchanges of one attention call at once: one p2p
+    launch, or on NCCL three pack launches and one group of send/recv for all
+    three tensors (instead of three all_to_all_single calls)."""
     if _p2p(ctx):
         return ctx.peer.fwd([q, k, v], ctx)
     s_local, heads, dim = q.shape
     hp = heads // ctx.world
-    outs, reqs = [], []
-    for t in (q, k, v):
-        send = pack(t, ctx.world).view(-1)
-        out = torch.empty(ctx.seq_len * hp * dim, dtype=t.dtype, device=t.device)
-        reqs.append((_seq_gather(out, send, ctx, hp * dim, async_op=True), send))
-        outs.append(out.view(ctx.seq_len, hp, dim))
-    for work, _ in reqs:
-        work.wait()
-    return outs
+    sends = [pack(t, ctx.world).view(-1) for t in (q, k, v)]
+    outs = [torch.empty(ctx.seq_len * hp * dim, dtype=q.dtype, device=q.device) for _ in range(3)]
+    with span("a2a_nccl_group", 3 * s_local * hp * dim * q.element_size() * (ctx.world - 1), launches=0):
+        for work in _seq_gather_group(outs, sends, ctx, hp * dim):
+            work.wait()
+    del sends  # the waits above order their reuse after the transfers
+    return [o.view(ctx.seq_len, hp, dim) for o in outs]
 
 
 def a2a_scatter_seq_gather_heads(t, ctx):
@@ -244,11 +277,24 @@ class PeerExchange:
     """Persistent IPC-mapped buffers and flags for the fused p2p all-to-all.
 
     Collective to construct (every rank of `group` calls it with the same
-    arguments) and to `close()`.  Buffers: n_fwd receive buffers of
-    [seq_len, chunk], one inverse output buffer of [max_local, world*chunk],
+    arguments) and to `close()`.  Buffers: two sets of n_fwd receive buffers
+    of [seq_len, chunk], one inverse output buffer of [max_local, world*chunk],
     one attention output buffer of [seq_len, chunk] that the peers read
     (inv_quant) (chunk = heads/world * head_dim elements), plus a uint32
     [world] flag array.
+
+    Barriers.  The block's exchange pair -- gemm_fwd (the qkv projection
+    storing into the owners' receive buffers) then inv_quant (the out
+    projection's quantiser gathering every rank's attention output) -- needs
+    two flag barriers per attention when it repeats: gemm_fwd alternates
+    between the two receive sets, so when it directly follows an inv_quant
+    it skips its entry barrier.  That is safe because a peer starts the next
+    gemm_fwd only after passing the inv_quant barrier, which every rank
+    reaches after its attention read the receive set written two exchanges
+    back; and a rank refills its attention output buffer only after the next
+    gemm_fwd's exit barrier, which every peer reaches after its gather of that
+    buffer.  Any other call sequence (fwd, inv, the overlap, a first call)
+    takes the entry barriers.
     """
 
     def __init__(self, group, rank, world, seq_len, heads, head_dim, dtype=torch.bfloat16, n_fwd=3,
@@ -264,14 +310,18 @@ class PeerExchange:
         max_local = -(-seq_len // world)
         timeout_s = float(os.environ.get("H3B_PEER_TIMEOUT_S", "30")) if timeout_s is None else timeout_s
         self.timeout_ns = int(timeout_s * 1e9)
-        self.recv = [torch.empty((seq_len, self.chunk), dtype=dtype, device=dev) for _ in range(n_fwd)]
+        self.recv_sets = [[torch.empty((seq_len, self.chunk), dtype=dtype, device=dev) for _ in range(n_fwd)]
+                          for _ in range(2)]
+        self.recv = self.recv_sets[0]  # the set fwd() and the overlap use
         self.out = torch.empty((max_local, world * self.chunk), dtype=dtype, device=dev)
         self.obuf = torch.empty((seq_len, self.chunk), dtype=dtype, device=dev)  # attention output, pulled by peers
         self.flags = torch.zeros(world, dtype=torch.int32, device=dev)
         self.epoch = 0
+        self.n_gemm_fwd = 0  # gemm_fwd calls so far: call k uses receive set k % 2
+        self._last = None  # "gemm_fwd" / "inv_quant" when the last call was one of the chained pair
         self.comm = None  # side stream of the exchange/attention overlap
         self._bases = []
-        shared = self.recv + [self.out, self.obuf, self.flags]
+        shared = self.recv_sets[0] + self.recv_sets[1] + [self.out, self.obuf, self.flags]
         mine = [self._handle(t) for t in shared]
         gathered = [None] * world
         dist.all_gather_object(gathered, mine, group=group)
@@ -279,8 +329,9 @@ class PeerExchange:
         for j in range(world):
             for idx, (hb, off) in enumerate(gathered[j]):
                 peer[idx][j] = shared[idx].data_ptr() if j == rank else self._open(hb, off)
-        self.peer_recv = peer[:n_fwd]
-        self.peer_out, self.peer_obuf, self.peer_flags = peer[n_fwd], peer[n_fwd + 1], peer[n_fwd + 2]
+        self.peer_recv_sets = [peer[:n_fwd], peer[n_fwd:2 * n_fwd]]
+        self.peer_recv = self.peer_recv_sets[0]
+        self.peer_out, self.peer_obuf, self.peer_flags = peer[2 * n_fwd], peer[2 * n_fwd + 1], peer[2 * n_fwd + 2]
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
@@ -312,12 +363,13 @@ class PeerExchange:
             raise ValueError(f"{groups} groups do not divide the {hp} heads of a rank")
         return self.chunk // groups, hp // groups
 
-    def recv_views(self, n, ctx, g=0, groups=1):
-        """Views [S, hc, Dh] of head group g in the first n receive buffers.  Group
-        g of width w occupies elements [g*seq_len*w, (g+1)*seq_len*w) of a buffer."""
+    def recv_views(self, n, ctx, g=0, groups=1, rset=0):
+        """Views [S, hc, Dh] of head group g in the first n receive buffers of set
+        rset.  Group g of width w occupies elements [g*seq_len*w, (g+1)*seq_len*w)
+        of a buffer."""
         w, hc = self._group(groups)
         base = g * self.seq_len * w
-        return [self.recv[i].view(-1)[base: base + ctx.seq_len * w].view(ctx.seq_len, hc, self.head_dim)
+        return [self.recv_sets[rset][i].view(-1)[base: base + ctx.seq_len * w].view(ctx.seq_len, hc, self.head_dim)
                 for i in range(n)]
 
     def fwd_copy(self, tensors, ctx, g=0, groups=1):
@@ -364,15 +416,20 @@ class PeerExchange:
             raise ValueError("gemm_fwd: the projection does not match the PeerExchange buffers")
         if xq.shape[0] != ctx.local:
             raise ValueError("gemm_fwd: xq must hold this rank's rows")
-        dst = [self.peer_recv[t][j] for t in range(nseg) for j in range(self.world)]
-        self.barrier(xq)
+        rset = self.n_gemm_fwd % 2
+        dst = [self.peer_recv_sets[rset][t][j] for t in range(nseg) for j in range(self.world)]
+        if self._last != "inv_quant":
+            self.barrier(xq)  # entry: every rank's receive set is free (not needed in the chained pair)
         int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst, ctx.start, D, self.head_dim, self.heads // self.world,
                            self.world, norm_w=norm_w, norm_eps=norm_eps)
-        self.barrier(xq)
-        return self.recv_views(nseg, ctx)
+        self.barrier(xq)  # exit: every rank's rows have arrived
+        self.n_gemm_fwd += 1
+        self._last = "gemm_fwd"
+        return self.recv_views(nseg, ctx, rset=rset)
 
     def fwd(self, tensors, ctx):
         """tensors: n x [s_local, H, D] -> n views [S, H/P, D] of the receive buffers."""
+        self._last = None
         self.barrier(tensors[0])
         self.fwd_copy(tensors, ctx)
         self.barrier(tensors[0])
@@ -397,6 +454,7 @@ class PeerExchange:
 
     def inv(self, t, ctx):
         """t [S, (H/P)*D] (unit stride along the row) -> [s_local, H*D] view of the output buffer."""
+        self._last = None
         self.barrier(t)
         self.inv_copy(t, ctx)
         self.barrier(t)
@@ -417,6 +475,8 @@ class PeerExchange:
         S, hp = ctx.seq_len, self.heads // self.world
         if S > self.seq_len:
             raise ValueError("inv_quant: sequence longer than the PeerExchange buffers")
+        if self._last != "gemm_fwd":
+            self.barrier(o)  # the peers' gathers of the previous contents are done
         self.obuf[:S].view(S, hp, self.head_dim).copy_(o.reshape(S, hp, self.head_dim))
         self.barrier(o)
         K = self.heads * self.head_dim
@@ -428,6 +488,7 @@ class PeerExchange:
             check(lib.h3b_a2a_inv_quant(arr, self.chunk * es, ctx.start, ctx.local, self.chunk * es, self.world,
                                         ptr(xq), ptr(xs), stream_of(o)), "h3b_a2a_inv_quant")
         del keep
+        self._last = "inv_quant"
         return xq, xs
 
     def attention_overlap(self, q, k, v, ctx, attn, groups):
@@ -438,6 +499,7 @@ class PeerExchange:
         everywhere); the attention of group g waits for that, and its inverse
         copy waits for the attention.  One last barrier: every rank's output
         buffer is complete.  Returns [s_local, H*D], a view of the output buffer."""
+        self._last = None
         cur = torch.cuda.current_stream(q.device)
         if self.comm is None:
             self.comm = torch.cuda.Stream(device=q.device, priority=-100)

@@ -61,6 +61,17 @@ def _worker_exchange(rank, world, port, S, q):
         sp._seq_gather(out, send, ctx, hp * Dh)
         ref = sp_layout.a2a_fwd(bits, world)[rank]
         np.testing.assert_array_equal(out.numpy().view(np.uint16).reshape(S, hp, Dh), ref)
+        # q, k, v as one group of point-to-point transfers (the NCCL path of a2a_gather_qkv)
+        trio = [[torch.randn(n, H, Dh, generator=torch.Generator().manual_seed(300 + 10 * i + r)).to(torch.bfloat16)
+                 for r, n in enumerate(ctx.splits)] for i in range(3)]
+        tbits = [[t.view(torch.int16).numpy().view(np.uint16) for t in ts3] for ts3 in trio]
+        sends = [torch.from_numpy(sp_layout.pack_fwd(tb[rank], world).view(np.float16)).reshape(-1) for tb in tbits]
+        outs3 = [torch.empty(S * hp * Dh, dtype=torch.float16) for _ in range(3)]
+        for work in sp._seq_gather_group(outs3, sends, ctx, hp * Dh):
+            work.wait()
+        for i in range(3):
+            np.testing.assert_array_equal(outs3[i].numpy().view(np.uint16).reshape(S, hp, Dh),
+                                          sp_layout.a2a_fwd(tbits[i], world)[rank])
         # inverse: each rank's [S, hp*Dh] -> [s_local, H*Dh] after unpack (oracle)
         outs = [torch.randn(S, hp * Dh, generator=torch.Generator().manual_seed(200 + r)).to(torch.bfloat16)
                 for r in range(world)]
@@ -172,3 +183,56 @@ def test_overlap_groups_env(monkeypatch):
     assert sp.overlap_groups(10, 4) == 5
     monkeypatch.setenv("H3B_SP_OVERLAP_GROUPS", "5")
     assert sp.overlap_groups(5, 8) == 5
+
+
+def test_peer_exchange_barrier_sequence(monkeypatch):
+    """Host logic of the p2p exchange pair (no device work: kernels stubbed).
+    gemm_fwd alternates between the two receive sets and skips its entry
+    barrier only right after inv_quant; inv_quant takes an extra entry
+    barrier unless it follows gemm_fwd; any other exchange call breaks the
+    chain.  Every rank runs the same sequence, so all ranks take the same
+    barriers."""
+    import importlib
+    import types
+
+    hl = importlib.import_module("h3b.linear")  # the module (h3b.linear is also a function name)
+    hsp = importlib.import_module("h3b.sp")
+
+    events = []
+    pe = object.__new__(hsp.PeerExchange)
+    pe.world, pe.rank, pe.heads, pe.head_dim, pe.chunk, pe.seq_len = 2, 0, 4, 64, 128, 16
+    pe.n_gemm_fwd, pe._last, pe.dtype = 0, None, torch.bfloat16
+    pe.recv_sets = [[torch.zeros(16, 128, dtype=torch.bfloat16) for _ in range(3)] for _ in range(2)]
+    pe.recv = pe.recv_sets[0]
+    pe.peer_recv_sets = [[[100 * s + 10 * t + j for j in range(2)] for t in range(3)] for s in range(2)]
+    pe.obuf = torch.zeros(16, 128, dtype=torch.bfloat16)
+    pe.peer_obuf = [1, 2]
+    pe.barrier = lambda t: events.append("B")
+    monkeypatch.setattr(hsp, "require_cuda", lambda *a: None)
+    monkeypatch.setattr(hsp, "stream_of", lambda t: None)
+    monkeypatch.setattr(hsp, "ptr", lambda t: 0)
+    monkeypatch.setattr(hsp, "lib", types.SimpleNamespace(h3b_a2a_inv_quant=lambda *a: events.append("Q") or 0))
+    monkeypatch.setattr(hl, "int8_mm_scaled_a2a",
+                        lambda xq, w, xs, ws, b, dst, *a, **k: events.append(("G", dst[0] // 100)))
+    ctx = types.SimpleNamespace(seq_len=16, local=8, start=0)
+    xq = torch.zeros(8, 256, dtype=torch.int8)
+    w = torch.zeros(3 * 256, 256, dtype=torch.int8)
+    o = torch.zeros(16, 128, dtype=torch.bfloat16)
+
+    def gemm():
+        pe.gemm_fwd(xq, None, w, None, None, ctx)
+
+    gemm()
+    pe.inv_quant(o, ctx)
+    gemm()
+    pe.inv_quant(o, ctx)
+    gemm()
+    pe.inv_quant(o, ctx)
+    assert events == ["B", ("G", 0), "B", "B", "Q",     # first pair: entry, exit, inverse
+                      ("G", 1), "B", "B", "Q",          # chained: no entry barrier, other set
+                      ("G", 0), "B", "B", "Q"]
+    events.clear()
+    pe.inv_quant(o, ctx)  # not after gemm_fwd: entry barrier before refilling the shared buffer
+    pe._last = None  # e.g. fwd() / the overlap ran in between
+    gemm()
+    assert events == ["B", "B", "Q", "B", ("G", 1), "B"]

@@ -137,6 +137,48 @@ def test_gelu_quant_equals_torch_gelu_then_quant(M, K, scale):
     assert torch.equal(q, q_ref), f"{(q != q_ref).sum().item()} codes differ"
 
 
+def _all_bf16():
+    """Every bf16 bit pattern once (zeros, subnormals, normals, infinities, NaNs)."""
+    return torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+
+
+def test_gelu_every_bf16_input_equals_torch():
+    """The fast GELU (x / (1 + 2^w) with an error margin, PyTorch's formula only
+    near a bf16 rounding midpoint) against F.gelu(approximate="tanh") on the GPU
+    for all 65536 bf16 inputs: a bf16 -> bf16 function is fully determined by
+    these, so equality here is equality everywhere.  NaN inputs must give NaN."""
+    import torch.nn.functional as F
+    x = _all_bf16().to(DEV)
+    y = h3b.gelu_tanh(x)
+    ref = F.gelu(x, approximate="tanh")
+    torch.cuda.synchronize()
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(y), nan)
+    bad = (y.view(torch.int16) != ref.view(torch.int16)) & ~nan
+    assert bad.sum().item() == 0, f"{bad.sum().item()} inputs differ, e.g. bits {torch.nonzero(bad)[:8].flatten().tolist()}"
+    # the odd-length tail of a call (n % 8 != 0) takes the pair path
+    y2 = h3b.gelu_tanh(x[:1030].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(y2.view(torch.int16), y[:1030].view(torch.int16))
+
+
+def test_gelu_quant_every_bf16_input():
+    """The GELU quantiser over rows that hold every finite bf16 value (shuffled,
+    one huge-magnitude row group and one small one) == quant_rowwise(F.gelu(row))."""
+    import torch.nn.functional as F
+    x = _all_bf16()
+    x = x[torch.isfinite(x.float())]
+    perm = torch.randperm(x.numel(), generator=gen(3))
+    x = x[perm][: (x.numel() // 512) * 512].view(-1, 512).to(DEV)
+    small = x.float().abs() < 4
+    xs = torch.where(small, x, torch.zeros_like(x))  # rows without the huge values: small absmax, fine codes
+    for u in (x, xs):
+        q, s = h3b.gelu_quant(u.contiguous())
+        q_ref, s_ref = h3b.quant_rowwise(F.gelu(u, approximate="tanh"))
+        torch.cuda.synchronize()
+        assert torch.equal(s, s_ref) and torch.equal(q, q_ref)
+
+
 def test_quant_half_integer_ties():
     """Rows whose quotients land exactly on (or next to) half-integers exercise the
     exact-division fallback; codes must match the oracle (round half to even)."""
