@@ -63,7 +63,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["dit_block", "dit_step", "linear", "fused", "a2a", "qkv_a2a", "quant",
-                                           "vs_triton", "nvlink_probe"],
+                                           "vs_triton", "nvlink_probe", "gemm"],
                     default="dit_block")
     ap.add_argument("--peers", type=int, default=8, help="ranks emulated by the qkv_a2a workload")
     ap.add_argument("--qknorm", action="store_true", help="qkv_a2a workload: with the per-head q/k RMSNorm")
@@ -624,6 +624,32 @@ def quant_workload(args, dev):
     return M, K, ms, clocks, tr.summary(args.steps), tr.launches / args.steps
 
 
+def gemm_workload(args, dev):
+    """The block's four INT8 GEMM shapes alone (qkv 5120->15360, out 5120->5120,
+    up 5120->13824, down 13824->5120) at M rows (default 128000, the benchmark
+    block), with bias, each launch timed with CUDA events after a 256 MB L2
+    flush; returns [(name, M, N, K, ms)].  Inputs are drawn on the device
+    (timing only)."""
+    import h3b
+    M = args.rows or 128000
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = []
+    for name, N, K in (("qkv", 15360, 5120), ("out", 5120, 5120), ("up", 13824, 5120), ("down", 5120, 13824)):
+        g = torch.Generator(device=dev).manual_seed(N + K)
+        xq = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8, device=dev)
+        xs = torch.rand(M, 1, generator=g, device=dev) * 0.05 + 1e-3
+        w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8, device=dev)
+        ws = torch.rand(N, generator=g, device=dev) * 9e-3 + 1e-3
+        b = (torch.randn(N, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        ms = _event_time(lambda: h3b.int8_mm_scaled(xq, w, xs, ws, out=y, bias=b), args.steps, flush,
+                         warmup=args.warmup)
+        out.append((name, M, N, K, ms))
+        del xq, xs, w, ws, b, y
+        torch.cuda.empty_cache()
+    return out
+
+
 def qkv_a2a_workload(args, dev):
     """One rank's qkv projection with the forward exchange in the GEMM's epilogue
     (h3b_int8_mm_scaled_a2a), on one GPU: the P ranks' receive buffers are all
@@ -1056,6 +1082,20 @@ def main():
                                "l2": "256 MB flush per step"},
                     "roofline": rl, "clocks": clocks, "gpu_launches": int(round(launches * args.steps)),
                     "breakdown": breakdown(spans, pk)}
+        elif args.workload == "gemm":
+            res = gemm_workload(args, dev)
+            peak = 2.0 * pk["bf16_tflops"]
+            shapes = [{"shape": n, "M": M, "N": N, "K": K, "ms": round(ms, 4),
+                       "tops": round(2.0 * M * N * K / ms / 1e9, 1),
+                       "frac_of_2x_bf16_burst": round(2.0 * M * N * K / ms / 1e9 / peak, 4)} for n, M, N, K, ms in res]
+            tot_ms = sum(r[4] for r in res)
+            tot_ops = sum(2.0 * r[1] * r[2] * r[3] for r in res)
+            line = {"metric": "block INT8 GEMMs TOPS", "value": round(tot_ops / tot_ms / 1e9, 1), "unit": "TOPS",
+                    "ms_per_step": round(tot_ms, 4), "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                    "higher_is_better": True, "dtype": "int8",
+                    "config": {"workload": "gemm", "M": res[0][1], "group_m": os.environ.get("H3B_GEMM_GROUP_M"),
+                               "l2": "256 MB flush before each launch"},
+                    "shapes": shapes}
         elif args.workload == "nvlink_probe":
             s_local, res, ok = nvlink_probe_workload(args)
             line = {"metric": "forward exchange over NVLink, one process driving 2 GPUs (GB/s of payload)",

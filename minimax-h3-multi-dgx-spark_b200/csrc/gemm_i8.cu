@@ -83,6 +83,7 @@ struct Args {
     int M, N, K;
     int* status;
     int tile_n;  // 2-CTA kernel: output tile width (multiple of 32, <= 256)
+    int group_m; // tile rows per group of the grouped-M raster
     Scatter sc;  // scatter epilogue only
     int act;     // bf16 output: 1 = GELU(tanh) applied to each rounded output value
 };
@@ -181,11 +182,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mb, int& nb) {
-    const int in_group = GROUP_M * n_tiles;
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int group_m, int& mb, int& nb) {
+    const int in_group = group_m * n_tiles;
     const int group = tile / in_group;
-    const int first_m = group * GROUP_M;
-    const int gsize = min(m_tiles - first_m, GROUP_M);
+    const int first_m = group * group_m;
+    const int gsize = min(m_tiles - first_m, group_m);
     const int r = tile % in_group;
     mb = first_m + r % gsize;
     nb = r / gsize;
@@ -414,7 +415,7 @@ const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
                 int mb, nb;
-                tile_coords(tile, m_tiles, n_tiles, mb, nb);
+                tile_coords(tile, m_tiles, n_tiles, args.group_m, mb, nb);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status)) {
                         ok = false;
@@ -495,7 +496,7 @@ const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB
         int t = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
             int mb, nb;
-            tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            tile_coords(tile, m_tiles, n_tiles, args.group_m, mb, nb);
             const int acc = t & 1;
             const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status)) break;
@@ -663,7 +664,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int tile = pair_id; ok && tile < num_tiles; tile += n_pairs) {
                 int mb, nb;
-                tile_coords(tile, m_tiles, n_tiles, mb, nb);
+                tile_coords(tile, m_tiles, n_tiles, args.group_m, mb, nb);
                 for (int kb = 0; kb < kblocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, args.status)) {
                         ok = false;
@@ -750,7 +751,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int t = 0;
         for (int tile = pair_id; tile < num_tiles; tile += n_pairs, ++t) {
             int mb, nb;
-            tile_coords(tile, m_tiles, n_tiles, mb, nb);
+            tile_coords(tile, m_tiles, n_tiles, args.group_m, mb, nb);
             const int acc = t & 1;
             const uint32_t acc_phase = (uint32_t)(t >> 1) & 1u;
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.status)) break;
@@ -852,6 +853,20 @@ static int num_sms() {
 // (rounds of pair tiles over the resident pairs) x (256 + t); ties go to the
 // wider tile.  Wave quantisation picks 224 for config 0's 4096 x 5120; large M
 // keeps 256.
+// Tile rows per group of the grouped-M raster (the weights are streamed once
+// per group).  H3B_GEMM_GROUP_M overrides it for tuning sweeps.
+static int pick_group_m(int K) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char* e = getenv("H3B_GEMM_GROUP_M");
+        const int v = e ? atoi(e) : 0;
+        forced = (v >= 1 && v <= 256) ? v : 0;
+    }
+    if (forced) return forced;
+    (void)K;
+    return GROUP_M;
+}
+
 static int pick_tile_n(int M, int N, int64_t pairs, int multiple = 32) {
     // H3B_GEMM_TILE_N (a multiple of 32 in 32..256) pins the width, for tuning sweeps
     static int forced = -1;
@@ -933,6 +948,7 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
         H3B_REQUIRE(!a.bias || aligned(a.bias, 16), "h3b GEMM: bias must be 16-byte aligned");
     }
     if (a.M == 0) return H3B_OK;
+    a.group_m = pick_group_m(a.K);
     if (int rc = check_device()) return rc;
     CUtensorMap tmA, tmB;
     if (int rc = make_map(&tmA, xq, a.M, a.K, BM)) return rc;
