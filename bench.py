@@ -323,18 +323,19 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup,
     if e2e_steps:
         e_host = [p.e.detach().cpu().pin_memory() for p in dit.params]
 
-        def load_tables():
-            for p, eh in zip(dit.params, e_host):
-                p.e.copy_(eh, non_blocking=True)
+        def load_tables(cond=None):
+            # the step's adaLN conditioning: from its device copies (pipelined) or from the host (serial)
+            for p, e in zip(dit.params, cond if cond is not None else e_host):
+                p.e.copy_(e, non_blocking=True)
                 p.tables = h3b.modulation_tables(*(p.e[:, i] for i in range(6)))
 
-        # pipelined: HostPipeline, input copy of step k+1 / output copy of step
-        # k-1 on copy streams during step k (three device slots)
+        # pipelined: HostPipeline, input copy (latent rows and conditioning) of step k+1 / output copy
+        # of step k-1 on copy streams during step k (three device slots)
         pipe = hm.HostPipeline(dit, s_local, ridx, ctx, text, depth=3, timing=True)
         outs = [torch.empty_like(x_host).pin_memory() for _ in range(3)]
 
         def step_pipe():
-            pipe.submit(x_host, outs[pipe.k % 3], before=load_tables)
+            pipe.submit(x_host, outs[pipe.k % 3], before=load_tables, cond_host=e_host)
 
         ms_e2e, _ = timed(step_pipe, e2e_steps, 1 if serial else 0, world, dev, sample_clocks=False,
                           finish=pipe.flush)

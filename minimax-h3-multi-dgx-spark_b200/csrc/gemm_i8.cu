@@ -18,9 +18,9 @@
 //               after each product), round once to bf16, store; then release
 //               the accumulator so the MMA warp can start the tile after next
 //               while this one drains.
-// Tiles are visited in the reference's grouped-M order (GROUP_M = 8,
-// int8_gemm_triton.py:37-45) so CTAs running at the same time share A and B
-// rows in L2.  Every mbarrier wait is bounded; on expiry the kernel records
+// Tiles are visited in the reference's grouped-M order (int8_gemm_triton.py:37-45,
+// GROUP_M = 8 there; 16 tile rows per group here, chosen by measurement) so
+// CTAs running at the same time share A and B rows in L2.  Every mbarrier wait is bounded; on expiry the kernel records
 // H3B_STATUS_MBAR_TIMEOUT, stops issuing work, drains its own TMA loads and
 // MMAs (again bounded), frees TMEM and returns.
 #include <mutex>
@@ -43,7 +43,7 @@ constexpr int TMEM_COLS = NUM_ACC * BN;  // 512: the whole TMEM of the SM
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 16;  // tile rows per group of the grouped-M raster
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr uint64_t kTimeoutNs = 10ull * 1000 * 1000 * 1000;
@@ -863,6 +863,9 @@ static int pick_group_m(int K) {
         forced = (v >= 1 && v <= 256) ? v : 0;
     }
     if (forced) return forced;
+    // 16 tile rows per group: measured on the block's four shapes at M=128000,
+    // 2-4% faster than 8 on each (the weights are streamed half as often) and
+    // faster than 32 (whose A slabs no longer stay in L2 for K=13824)
     (void)K;
     return GROUP_M;
 }

@@ -217,12 +217,27 @@ __device__ __forceinline__ bool bar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in the instruction
+// until the phase completes or about 0.1 ms pass, instead of spinning and
+// taking issue slots from the warps that compute.
+__device__ __forceinline__ bool bar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(100000u)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool bar_wait_parity_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
     if (bar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (uint32_t n = 1;; ++n) {
-        if (bar_try_wait(bar, parity)) return true;
-        if ((n & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    for (;;) {
+        if (bar_try_wait_sleep(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 
@@ -287,19 +302,15 @@ __device__ __forceinline__ uint4 lut8(const uint16_t* lut, uint4 v) {
 
 // Rows r = blockIdx.x, + gridDim.x, ...: up to kMaxRowBufs rows ahead are in
 // flight as bulk copies into shared-memory row buffers (one mbarrier each),
-// so the bytes in flight per SM do not depend on registers.  Thread t owns
-// vectors t, t + 1024, .. of every row.  Per row, each warp looks its vectors
-// up, reduces their absmax and posts it (a per-warp slot and one arrival on
-// the row's max barrier, four of each in rotation: a warp posts row i + 1
-// only after row i - 1 is complete, and every warp read row i - 3's slot
-// before posting row i - 1, so the slot row i + 1 reuses is free); it then
-// looks up the NEXT row before waiting for the current row's barrier, so a
-// late warp holds the others back by at most a row instead of at every row.
-// A completed max barrier also means every warp has read the row's buffer:
-// thread 0 requests the buffer's next row there.  Codes are written from
-// registers.
+// so the bytes in flight per SM do not depend on registers.  (Replacing the
+// per-row CTA barrier with per-row mbarriers and looking the next row up
+// before the current row's maximum was measured slower: 0.445 vs 0.419 ms at
+// M=32768, the waiting warps' polling taking issue slots.)  Per row: wait
+// for its buffer, thread t takes vectors t, t + 1024, .. into registers,
+// looks them up, takes the absmax; one barrier per row (the per-warp maxima
+// alternate between two shared arrays) also frees the buffer, whose next row
+// thread 0 then requests; codes are written from the registers.
 constexpr int kMaxRowBufs = 3;
-constexpr int kMaxSlots = 4;
 
 template <int VPT>
 __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const uint16_t* __restrict__ x, int64_t ldx,
@@ -309,49 +320,50 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
     extern __shared__ __align__(128) uint16_t lut[];  // 65536 table entries, then nbuf rows of K
     __shared__ __align__(8) uint64_t bar;
     __shared__ __align__(8) uint64_t full[kMaxRowBufs];
-    __shared__ __align__(8) uint64_t maxbar[kMaxSlots];
-    __shared__ uint32_t wmax[kMaxSlots][kLutThreads / 32];
-    constexpr uint64_t kLimit = 10ull * 1000 * 1000 * 1000;
+    __shared__ uint32_t wmax[2][kLutThreads / 32];
     const int nvec = K >> 3;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int t = threadIdx.x;
     const uint32_t row_bytes = (uint32_t)K * 2u;
     uint4* rows = reinterpret_cast<uint4*>(lut + 65536);
     const int64_t step = gridDim.x;
-    auto sa = [](const void* p) { return (uint32_t)__cvta_generic_to_shared(p); };
     auto request = [&](int b, int64_t r) {  // thread 0 only
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(&full[b])), "r"(row_bytes)
-                     : "memory");
+        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sb), "r"(row_bytes) : "memory");
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                sa(rows + (int64_t)b * nvec)),
-            "l"(x + r * ldx), "r"(row_bytes), "r"(sa(&full[b]))
+                (uint32_t)__cvta_generic_to_shared(rows + (int64_t)b * nvec)),
+            "l"(x + r * ldx), "r"(row_bytes), "r"(sb)
             : "memory");
     };
-    // the copies that may still be in flight when this CTA gives up: its rows
-    // first .. first + nbuf - 1 (row k of this CTA is its k-th)
-    auto drain = [&](int first) {
-        if (t == 0)
-            for (int k = first; k < first + nbuf && blockIdx.x + k * step < M; ++k)
-                bar_wait_parity_bounded(sa(&full[k % nbuf]), (uint32_t)((k / nbuf) & 1), 100ull * 1000 * 1000);
-    };
     if (t == 0) {
-        for (int b = 0; b < nbuf; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sa(&full[b])) : "memory");
-        for (int k = 0; k < kMaxSlots; ++k)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(&maxbar[k])), "r"(kLutThreads / 32)
+        for (int b = 0; b < nbuf; ++b)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&full[b]))
                          : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         for (int b = 0; b < nbuf; ++b)
             if (blockIdx.x + b * step < M) request(b, blockIdx.x + b * step);
     }
-    if (!load_table(lut, &bar, status)) {  // includes a barrier: the inits above are visible after it
-        drain(0);
+    if (!load_table(lut, &bar, status)) {
+        if (t == 0)
+            for (int b = 0; b < nbuf; ++b)
+                if (blockIdx.x + b * step < M) bar_wait_bounded((uint32_t)__cvta_generic_to_shared(&full[b]),
+                                                                100ull * 1000 * 1000);
         return;
     }
-    // look this CTA's k-th row up into v and post its per-warp max; false on a timeout
-    auto lookup = [&](int k, uint4 (&v)[VPT]) -> bool {
-        const int b = k % nbuf;
-        if (!bar_wait_parity_bounded(sa(&full[b]), (uint32_t)((k / nbuf) & 1), kLimit)) return false;
+    int it = 0;
+    for (int64_t row = blockIdx.x; row < M; row += step, ++it) {
+        const int b = it % nbuf;
+        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
+        if (!bar_wait_parity_bounded(sb, (uint32_t)((it / nbuf) & 1), 10ull * 1000 * 1000 * 1000)) {
+            report(status, H3B_STATUS_MBAR_TIMEOUT);
+            if (t == 0)  // the copies this CTA still has in flight, before its shared memory goes
+                for (int k = 0; k < nbuf && row + k * step < M; ++k)
+                    bar_wait_parity_bounded((uint32_t)__cvta_generic_to_shared(&full[(it + k) % nbuf]),
+                                            (uint32_t)(((it + k) / nbuf) & 1), 100ull * 1000 * 1000);
+            return;
+        }
         const uint4* rb = rows + (int64_t)b * nvec;
+        uint4 v[VPT];
         uint32_t m = 0;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
@@ -363,36 +375,10 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
         }
         uint32_t mb = max(m & 0xFFFFu, m >> 16);
         mb = __reduce_max_sync(0xffffffffu, mb);
-        if (lane == 0) {
-            wmax[k % kMaxSlots][warp] = mb;
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(&maxbar[k % kMaxSlots])) : "memory");
-        }
-        __syncwarp();
-        return true;
-    };
-    uint4 cur[VPT], nxt[VPT];
-    int it = 0;
-    int64_t row = blockIdx.x;
-    if (row < M && !lookup(0, cur)) {
-        report(status, H3B_STATUS_MBAR_TIMEOUT);
-        drain(0);
-        return;
-    }
-    for (; row < M; row += step, ++it) {
-        const bool more = row + step < M;
-        const bool ahead = more && nbuf >= 2;  // with one buffer the next row comes in only after this one
-        if (ahead && !lookup(it + 1, nxt)) {
-            report(status, H3B_STATUS_MBAR_TIMEOUT);
-            drain(it + 1);
-            return;
-        }
-        if (!bar_wait_parity_bounded(sa(&maxbar[it % kMaxSlots]), (uint32_t)((it / kMaxSlots) & 1), kLimit)) {
-            report(status, H3B_STATUS_MBAR_TIMEOUT);
-            drain(it + 1);
-            return;
-        }
-        if (t == 0 && row + nbuf * step < M) request(it % nbuf, row + nbuf * step);
-        const uint32_t mb = __reduce_max_sync(0xffffffffu, wmax[it % kMaxSlots][lane]);
+        if ((t & 31) == 0) wmax[it & 1][t >> 5] = mb;
+        __syncthreads();  // every thread has read buffer b: its next row may come in
+        if (t == 0 && row + nbuf * step < M) request(b, row + nbuf * step);
+        mb = __reduce_max_sync(0xffffffffu, wmax[it & 1][t & 31]);
         float s, rc;
         row_scale(__uint_as_float(mb << 16), s, rc);
         if (t == 0) xs[row] = s;
@@ -402,17 +388,10 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
             const int j = t + i * kLutThreads;
             if (j < nvec) {
                 float f[8];
-                unpack8(cur[i], f);
+                unpack8(v[i], f);
                 qr[j] = quant8(f, s, rc);
             }
         }
-        if (more && !ahead && !lookup(it + 1, nxt)) {
-            report(status, H3B_STATUS_MBAR_TIMEOUT);
-            drain(it + 1);
-            return;
-        }
-#pragma unroll
-        for (int i = 0; i < VPT; ++i) cur[i] = nxt[i];
     }
 }
 

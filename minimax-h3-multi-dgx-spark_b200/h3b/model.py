@@ -283,6 +283,7 @@ class HostPipeline:
         self.k = 0
         self.timing = timing
         self._ev = {"in": [], "out": []}
+        self.cond_slots = [None] * depth  # per-slot device copies of the step's conditioning
 
     def _timed_copy(self, kind, stream, dst, src):
         if not self.timing:
@@ -299,19 +300,31 @@ class HostPipeline:
         torch.cuda.synchronize(self.device)
         return {k: (sum(a.elapsed_time(b) for a, b in v) / len(v) if v else None) for k, v in self._ev.items()}
 
-    def submit(self, x_host, out_host, before=None):
+    def submit(self, x_host, out_host, before=None, cond_host=None):
+        """One step.  cond_host (optional): pinned host tensors of per-step
+        conditioning (e.g. the adaLN vectors); they are copied on the input copy
+        stream into this slot's own device buffers, like x, and `before` is then
+        called with the device copies (before(cond_dev)), so the compute stream
+        issues no host copy that could queue behind another step's input copy."""
         i = self.k % len(self.slots)
         slot = self.slots[i]
         cur = torch.cuda.current_stream(self.device)
+        cond_dev = None
         with torch.cuda.stream(self.copy_in):
             if self.freed[i] is not None:
                 self.copy_in.wait_event(self.freed[i])
             self._timed_copy("in", self.copy_in, slot, x_host)
+            if cond_host is not None:
+                if self.cond_slots[i] is None:
+                    self.cond_slots[i] = [torch.empty(c.shape, dtype=c.dtype, device=self.device) for c in cond_host]
+                cond_dev = self.cond_slots[i]
+                for d, c in zip(cond_dev, cond_host):
+                    d.copy_(c, non_blocking=True)
             ready = torch.cuda.Event()
             ready.record(self.copy_in)
         cur.wait_event(ready)
         if before is not None:
-            before()
+            before() if cond_host is None else before(cond_dev)
         y = self.model.forward(slot, self.ridx, self.ctx, self.text)
         done = torch.cuda.Event()
         done.record(cur)

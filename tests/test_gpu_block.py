@@ -80,6 +80,34 @@ def test_host_pipeline_matches_serial_steps():
         assert torch.equal(outs[k].view(torch.int16), ref.view(torch.int16)), f"step {k} differs"
 
 
+def test_host_pipeline_with_per_step_conditioning():
+    """Per-step adaLN conditioning through HostPipeline's input copy stream
+    (cond_host -> the slot's device copies -> `before`): each step's output
+    equals a serial forward with that step's conditioning loaded first."""
+    cfg = hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816, n_blocks=2)
+    S = 1200
+    dit = hm.SynthDiT(cfg, DEV, seed=10)
+    ridx = torch.zeros(S, dtype=torch.int32, device=DEV)
+    xs = [randn_bf16((S, cfg.dim), 60 + k).pin_memory() for k in range(4)]
+    es = [[randn_bf16(tuple(p.e.shape), 70 + 10 * k + b, 0.1).pin_memory() for b, p in enumerate(dit.params)]
+          for k in range(4)]
+    outs = [torch.empty(S, cfg.dim, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+
+    def load(cond):
+        for p, e in zip(dit.params, cond):
+            p.e.copy_(e, non_blocking=True)
+            p.tables = h3b.modulation_tables(*(p.e[:, i] for i in range(6)))
+    pipe = hm.HostPipeline(dit, S, ridx, depth=3)
+    for k in range(4):
+        pipe.submit(xs[k], outs[k], before=load, cond_host=es[k])
+    pipe.flush()
+    torch.cuda.synchronize()
+    for k in range(4):
+        load([e.to(DEV) for e in es[k]])
+        ref = dit.forward(xs[k].to(DEV), ridx).cpu()
+        assert torch.equal(outs[k].view(torch.int16), ref.view(torch.int16)), f"step {k} differs"
+
+
 def test_block_with_qk_norm():
     """The block with the per-head q/k RMSNorm (rms_norm kernel on the unfused path)."""
     _run(hm.DiTConfig(dim=1024, heads=8, head_dim=128, ffn=2816, qk_norm=True), S=1000, R=2, seed=6)
