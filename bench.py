@@ -787,13 +787,15 @@ def nvlink_probe_workload(args):
     def gemm():
         h3b.int8_mm_scaled_a2a(xq, w, xs, ws, bias, dst, 0, H * Dh, Dh, H // P, P)
     res = {}
+    ok = False
     for name, fn in (("a2a_fwd_p2p", copy), ("gemm_i8_scatter_qkv", gemm)):
         ms = _event_time(lambda: (fn(), torch.cuda.synchronize(d1)), args.steps, warmup=args.warmup)
         res[name] = {"ms": round(ms, 4), "nvlink_payload_bytes": off,
                      "nvlink_payload_gbs": round(off / ms / 1e6, 1)}
-    # the rows rank 1 received equal rank 0's own pack of its heads 20..39
-    ok = all(torch.equal(recv[i][1][:s_local].view(torch.int16),
-                         src[i].view(s_local, P, chunk)[:, 1].contiguous().to(d1).view(torch.int16)) for i in range(3))
+        if name == "a2a_fwd_p2p":  # before the GEMM overwrites the buffers: rank 1 holds heads 20..39 of rank 0's rows
+            ok = all(torch.equal(recv[i][1][:s_local].view(torch.int16),
+                                 src[i].view(s_local, P, chunk)[:, 1].contiguous().to(d1).view(torch.int16))
+                     for i in range(3))
     del k1, k2
     return s_local, res, ok
 

@@ -79,40 +79,6 @@ def _seq_scatter(out, send, ctx, width, async_op=False):
                                   group=ctx.group, async_op=async_op)
 
 
-def _seq_gather_group(outs, sends, ctx, width):
-    """_seq_gather of several tensors as ONE group of point-to-point transfers
-    (torch.distributed.batch_isend_irecv: one ncclGroupStart/End on NCCL): for
-    each tensor, this rank's chunk for rank j goes to j and rank j's rows land
-    at their place in the output; the own chunk is a local copy.  sends[i] is
-    [P * local * width] in destination order (the pack layout), outs[i] is
-    [S * width].  Returns the requests to wait on."""
-    ops = []
-    starts = [0]
-    for n in ctx.splits:
-        starts.append(starts[-1] + n)
-    me = ctx.rank
-    for out, send in zip(outs, sends):
-        src = send.view(ctx.world, ctx.local * width)
-        for j in range(ctx.world):
-            if j == me:
-                continue
-            ops.append(dist.P2POp(dist.isend, src[j], _global_rank(ctx, j), group=ctx.group))
-            ops.append(dist.P2POp(dist.irecv, out[starts[j] * width: starts[j + 1] * width], _global_rank(ctx, j),
-                                  group=ctx.group))
-    reqs = dist.batch_isend_irecv(ops) if ops else []
-    for out, send in zip(outs, sends):
-        out[starts[me] * width: starts[me + 1] * width].copy_(send.view(ctx.world, -1)[me])
-    return reqs
-
-
-def _global_rank(ctx, j):
-    """Global rank of group rank j (P2P ops name peers by global rank)."""
-    g = ctx.group
-    if g is None or g == dist.group.WORLD:
-        return j
-    return dist.get_global_rank(g, j)
-
-
 def _rows(t):
     """View t as [rows, row_elems] with unit element stride inside a row; returns (t2d, row stride)."""
     t2 = t.reshape(t.shape[0], -1) if t.dim() != 2 else t
@@ -181,19 +147,23 @@ def a2a_gather_seq_scatter_heads(t, ctx):
 
 def a2a_gather_qkv(q, k, v, ctx):
     """The three forward exchanges of one attention call at once: one p2p
-    launch, or on NCCL three pack launches and one group of send/recv for all
-    three tensors (instead of three all_to_all_single calls)."""
+    launch, or on NCCL three pack launches and three asynchronous
+    all_to_all_single calls.  (One group of point-to-point sends/receives for
+    all three tensors, batch_isend_irecv, measured 149 GB/s bus at P=2 against
+    341 GB/s for the all_to_all_single calls, and was dropped.)"""
     if _p2p(ctx):
         return ctx.peer.fwd([q, k, v], ctx)
     s_local, heads, dim = q.shape
     hp = heads // ctx.world
-    sends = [pack(t, ctx.world).view(-1) for t in (q, k, v)]
-    outs = [torch.empty(ctx.seq_len * hp * dim, dtype=q.dtype, device=q.device) for _ in range(3)]
-    with span("a2a_nccl_group", 3 * s_local * hp * dim * q.element_size() * (ctx.world - 1), launches=0):
-        for work in _seq_gather_group(outs, sends, ctx, hp * dim):
-            work.wait()
-    del sends  # the waits above order their reuse after the transfers
-    return [o.view(ctx.seq_len, hp, dim) for o in outs]
+    outs, reqs = [], []
+    for t in (q, k, v):
+        send = pack(t, ctx.world).view(-1)
+        out = torch.empty(ctx.seq_len * hp * dim, dtype=t.dtype, device=t.device)
+        reqs.append((_seq_gather(out, send, ctx, hp * dim, async_op=True), send))
+        outs.append(out.view(ctx.seq_len, hp, dim))
+    for work, _ in reqs:
+        work.wait()
+    return outs
 
 
 def a2a_scatter_seq_gather_heads(t, ctx):

@@ -61,17 +61,6 @@ def _worker_exchange(rank, world, port, S, q):
         sp._seq_gather(out, send, ctx, hp * Dh)
         ref = sp_layout.a2a_fwd(bits, world)[rank]
         np.testing.assert_array_equal(out.numpy().view(np.uint16).reshape(S, hp, Dh), ref)
-        # q, k, v as one group of point-to-point transfers (the NCCL path of a2a_gather_qkv)
-        trio = [[torch.randn(n, H, Dh, generator=torch.Generator().manual_seed(300 + 10 * i + r)).to(torch.bfloat16)
-                 for r, n in enumerate(ctx.splits)] for i in range(3)]
-        tbits = [[t.view(torch.int16).numpy().view(np.uint16) for t in ts3] for ts3 in trio]
-        sends = [torch.from_numpy(sp_layout.pack_fwd(tb[rank], world).view(np.float16)).reshape(-1) for tb in tbits]
-        outs3 = [torch.empty(S * hp * Dh, dtype=torch.float16) for _ in range(3)]
-        for work in sp._seq_gather_group(outs3, sends, ctx, hp * Dh):
-            work.wait()
-        for i in range(3):
-            np.testing.assert_array_equal(outs3[i].numpy().view(np.uint16).reshape(S, hp, Dh),
-                                          sp_layout.a2a_fwd(tbits[i], world)[rank])
         # inverse: each rank's [S, hp*Dh] -> [s_local, H*Dh] after unpack (oracle)
         outs = [torch.randn(S, hp * Dh, generator=torch.Generator().manual_seed(200 + r)).to(torch.bfloat16)
                 for r in range(world)]
