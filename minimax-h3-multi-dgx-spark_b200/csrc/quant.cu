@@ -302,31 +302,32 @@ __device__ __forceinline__ uint4 lut8(const uint16_t* lut, uint4 v) {
 
 // Rows r = blockIdx.x, + gridDim.x, ...: up to kMaxRowBufs rows ahead are in
 // flight as bulk copies into shared-memory row buffers (one mbarrier each),
-// so the bytes in flight per SM do not depend on registers.  (Replacing the
-// per-row CTA barrier with per-row mbarriers and looking the next row up
-// before the current row's maximum was measured slower: 0.445 vs 0.419 ms at
-// M=32768, the waiting warps' polling taking issue slots.)  Per row: wait
-// for its buffer, thread t takes vectors t, t + 1024, .. into registers,
-// looks them up, takes the absmax; one barrier per row (the per-warp maxima
-// alternate between two shared arrays) also frees the buffer, whose next row
-// thread 0 then requests; codes are written from the registers.
+// so the bytes in flight per SM do not depend on registers.
 constexpr int kMaxRowBufs = 3;
+
+// Two halves of 512 threads, each with its own rows (the CTA's even and odd
+// rows) and its own named barrier, so one half's barrier wait is covered by
+// the other half's lookups and stores.  The row buffers are shared: the half
+// that releases its row k requests row k + nbuf, which may be the other
+// half's.  Within a half: wait for the row's buffer, look it up, post the
+// per-warp maxima, one barrier, request, scale (every warp of the half), codes.
+constexpr int kHalfThreads = kLutThreads / 2;
 
 template <int VPT>
 __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const uint16_t* __restrict__ x, int64_t ldx,
-                                                                          int64_t M, int K, int8_t* __restrict__ xq,
-                                                                          float* __restrict__ xs, int nbuf,
-                                                                          int* status) {
+                                                                           int64_t M, int K, int8_t* __restrict__ xq,
+                                                                           float* __restrict__ xs, int nbuf,
+                                                                           int* status) {
     extern __shared__ __align__(128) uint16_t lut[];  // 65536 table entries, then nbuf rows of K
     __shared__ __align__(8) uint64_t bar;
     __shared__ __align__(8) uint64_t full[kMaxRowBufs];
-    __shared__ uint32_t wmax[2][kLutThreads / 32];
+    __shared__ uint32_t wmax[2][2][kHalfThreads / 32];  // [half][row parity][warp of the half]
     const int nvec = K >> 3;
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, h = t / kHalfThreads, th = t % kHalfThreads, lane = t & 31, hw = th >> 5;
     const uint32_t row_bytes = (uint32_t)K * 2u;
     uint4* rows = reinterpret_cast<uint4*>(lut + 65536);
     const int64_t step = gridDim.x;
-    auto request = [&](int b, int64_t r) {  // thread 0 only
+    auto request = [&](int b, int64_t r) {  // one thread
         const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sb), "r"(row_bytes) : "memory");
         asm volatile(
@@ -350,16 +351,17 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
                                                                 100ull * 1000 * 1000);
         return;
     }
-    int it = 0;
-    for (int64_t row = blockIdx.x; row < M; row += step, ++it) {
-        const int b = it % nbuf;
-        const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&full[b]);
-        if (!bar_wait_parity_bounded(sb, (uint32_t)((it / nbuf) & 1), 10ull * 1000 * 1000 * 1000)) {
+    // this half's rows: the CTA's k-th rows with k % 2 == h
+    for (int k = h; blockIdx.x + k * step < M; k += 2) {
+        const int64_t row = blockIdx.x + k * step;
+        const int b = k % nbuf;
+        if (!bar_wait_parity_bounded((uint32_t)__cvta_generic_to_shared(&full[b]), (uint32_t)((k / nbuf) & 1),
+                                     10ull * 1000 * 1000 * 1000)) {
             report(status, H3B_STATUS_MBAR_TIMEOUT);
-            if (t == 0)  // the copies this CTA still has in flight, before its shared memory goes
-                for (int k = 0; k < nbuf && row + k * step < M; ++k)
-                    bar_wait_parity_bounded((uint32_t)__cvta_generic_to_shared(&full[(it + k) % nbuf]),
-                                            (uint32_t)(((it + k) / nbuf) & 1), 100ull * 1000 * 1000);
+            if (th == 0)  // copies requested by this CTA that may still be in flight
+                for (int j = k; j < k + nbuf && blockIdx.x + j * step < M; ++j)
+                    bar_wait_parity_bounded((uint32_t)__cvta_generic_to_shared(&full[j % nbuf]),
+                                            (uint32_t)((j / nbuf) & 1), 100ull * 1000 * 1000);
             return;
         }
         const uint4* rb = rows + (int64_t)b * nvec;
@@ -367,7 +369,7 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
         uint32_t m = 0;
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-            const int j = t + i * kLutThreads;
+            const int j = th + i * kHalfThreads;
             if (j < nvec) {
                 v[i] = lut8(lut, rb[j]);
                 m = absmax_bits8(v[i], m);
@@ -375,17 +377,21 @@ __global__ void __launch_bounds__(kLutThreads, 1) gelu_quant_lut_kernel(const ui
         }
         uint32_t mb = max(m & 0xFFFFu, m >> 16);
         mb = __reduce_max_sync(0xffffffffu, mb);
-        if ((t & 31) == 0) wmax[it & 1][t >> 5] = mb;
-        __syncthreads();  // every thread has read buffer b: its next row may come in
-        if (t == 0 && row + nbuf * step < M) request(b, row + nbuf * step);
-        mb = __reduce_max_sync(0xffffffffu, wmax[it & 1][t & 31]);
+        // the maxima alternate between two slots by row, so one barrier per row
+        // suffices: a warp writes slot p again two rows later, after the next
+        // barrier, which every warp reaches only after reading slot p
+        const int p = (k >> 1) & 1;
+        if (lane == 0) wmax[h][p][hw] = mb;
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + h), "r"(kHalfThreads) : "memory");  // this half's row is read
+        if (th == 0 && row + nbuf * step < M) request(b, row + nbuf * step);
+        mb = __reduce_max_sync(0xffffffffu, wmax[h][p][lane & (kHalfThreads / 32 - 1)]);
         float s, rc;
         row_scale(__uint_as_float(mb << 16), s, rc);
-        if (t == 0) xs[row] = s;
+        if (th == 0) xs[row] = s;
         uint2* qr = reinterpret_cast<uint2*>(xq + row * (int64_t)K);
 #pragma unroll
         for (int i = 0; i < VPT; ++i) {
-            const int j = t + i * kLutThreads;
+            const int j = th + i * kHalfThreads;
             if (j < nvec) {
                 float f[8];
                 unpack8(v[i], f);
@@ -428,16 +434,10 @@ static int gelu_table_ready(cudaStream_t s) {
     if (dev < 0 || dev >= 64) return set_error(H3B_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
     Slot& slot = slots[dev];
     std::call_once(slot.once, [&slot, s] {
-        cudaError_t e = cudaFuncSetAttribute(gelu_quant_lut_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kLutSmemMax);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gelu_quant_lut_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gelu_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTableBytes);
+        cudaError_t e = cudaFuncSetAttribute(gelu_lut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTableBytes);
+        for (auto fn : {gelu_quant_lut_kernel<1>, gelu_quant_lut_kernel<2>, gelu_quant_lut_kernel<4>,
+                        gelu_quant_lut_kernel<8>})
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutSmemMax);
         if (e == cudaSuccess) {
             gelu_table_fill_kernel<<<128, 256, 0, s>>>();
             e = cudaGetLastError();
@@ -460,19 +460,17 @@ static int gelu_quant_lut(const uint16_t* x, int64_t ldx, int64_t M, int K, int8
     DeviceStatus ds;
     if (int rc = device_status(&ds)) return rc;
     const int nvec = K / 8;
-    const int vpt = (nvec + kLutThreads - 1) / kLutThreads;  // <= 4 for K <= 32768
     const int row_bytes = K * 2;
     int nbuf = (kLutSmemMax - kTableBytes) / row_bytes;  // >= 1 for K <= 32768
     if (nbuf > kMaxRowBufs) nbuf = kMaxRowBufs;
     const int smem = kTableBytes + nbuf * row_bytes;
     const int64_t sms = num_sms_here();
     const unsigned grid = (unsigned)(M < sms ? M : sms);
-    switch (vpt) {
-        case 1: gelu_quant_lut_kernel<1><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
-        case 2: gelu_quant_lut_kernel<2><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
-        case 3: gelu_quant_lut_kernel<3><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
-        default: gelu_quant_lut_kernel<4><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word); break;
-    }
+    const int v2 = (nvec + kHalfThreads - 1) / kHalfThreads;  // vectors per thread, <= 8 for K <= 32768
+    if (v2 <= 1) gelu_quant_lut_kernel<1><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word);
+    else if (v2 <= 2) gelu_quant_lut_kernel<2><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word);
+    else if (v2 <= 4) gelu_quant_lut_kernel<4><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word);
+    else gelu_quant_lut_kernel<8><<<grid, kLutThreads, smem, s>>>(x, ldx, M, K, xq, xs, nbuf, ds.word);
     H3B_CUDA_TRY(cudaGetLastError());
     return H3B_OK;
 }
