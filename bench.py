@@ -2,8 +2,10 @@
 """Benchmark of the H3 DiT hot path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload dit_block|dit_step|linear|fused|a2a|qkv_a2a] [--seq S] [--exchange p2p|nccl]
-                    [--overlap G] [--rows M] [--blocks B] [--convrot 64|256] [--qknorm] [--peers P]
+                    [--workload dit_block|dit_step|linear|fused|a2a|qkv_a2a|quant|gemm|vs_triton|nvlink_probe]
+                    [--seq S] [--exchange p2p|nccl] [--overlap G] [--rows M] [--cols K] [--act none|gelu]
+                    [--blocks B] [--convrot 64|256] [--qknorm] [--peers P]
+                    [--no-cpu-baseline] [--no-e2e] [--no-parity] [--no-step] [--no-a2a]
 
 Default workload (dit_block): one synthetic DiT block of the benchmark's
 block configuration -- D=5120, 40 heads x 128, FFN 13824 (GELU-tanh), four
@@ -25,11 +27,22 @@ copies and compute in sequence on one stream; `roofline` is the INT8 GEMM
 region; `cpu_baseline` times the reference's eager PyTorch path on the host's
 cores on a bounded sample of the same workload (rank 0, N=1 only).
 `--impl reference` prints the CPU reference path's line instead (rank 0 only).
-The other workloads (linear = single INT8 linear of config 0, fused = the
-fused chain of config 1, a2a = the Ulysses exchange of config 2, dit_step =
-the 40-block step of config 4, qkv_a2a = one rank's qkv GEMM with the forward
-exchange in its epilogue, the ranks' buffers emulated on one GPU) are
-available for measurements by hand.
+After every timed region a checker leg compares the timed path's output with
+the reference's eager path on the same rows (`parity`, bit for bit, summed over
+ranks; at N > 1 the eager exchange is all_to_all_single over NCCL).  The
+default line also carries `dit_step` (configuration 4: 40 blocks, S=252000,
+512 text tokens; one block forward of warm-up, 2 timed steps, 1 step end to
+end, and the final latent's parity) and, at N > 1, `a2a` (configuration 2 on
+both exchange back ends, bus GB/s, an identity round trip checked bit for bit,
+NVML's NVLink byte counters around the timed region).
+The other workloads are for measurements by hand: linear = single INT8 linear
+of config 0, fused = the fused chain of config 1, a2a = the Ulysses exchange of
+config 2, dit_step = the 40-block step alone, qkv_a2a = one rank's qkv GEMM with
+the forward exchange in its epilogue (the ranks' buffers emulated on one GPU),
+quant = the activation quantiser (--act gelu: the GELU quantiser), gemm = the
+block's four GEMM shapes, vs_triton = the reference's own Triton kernels against
+this library's on the same GPU, nvlink_probe = one process driving two GPUs
+through the forward exchange (for ncu's NVLink counters).
 """
 import argparse
 import json
@@ -575,9 +588,11 @@ def cpu_baseline(cfg, seq, steps=3, warmup=1):
     ref = CpuReference(cfg, seq)
     for _ in range(warmup):
         ref.run()
-    ms = statistics.median([ref.run() for _ in range(steps)])
+    runs = [ref.run() for _ in range(steps)]
+    ms = statistics.median(runs)
     return {"value": round(ms, 1), "unit": "ms/step", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": ref.sample()}
+            "sample": ref.sample(), "runs_ms": [round(r, 1) for r in runs],
+            "spread": round((max(runs) - min(runs)) / ms, 3)}
 
 
 # ---------------------------------------------------------------------------
@@ -1025,7 +1040,8 @@ def main():
         ref = CpuReference(cfg, seq)
         for _ in range(args.warmup):
             ref.run()
-        v = statistics.median([ref.run() for _ in range(args.steps)])
+        runs = [ref.run() for _ in range(args.steps)]
+        v = statistics.median(runs)
         sample, cores = ref.sample(), torch.get_num_threads()
         line = {"impl": "reference", "metric": "DiT fwd ms/step", "value": round(v, 1), "unit": "ms/step",
                 "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(v, 1),
@@ -1034,7 +1050,8 @@ def main():
                 "config": dit_config(cfg, "dit_block", seq, args.gpus, 1, 0, args.exchange),
                 "host": "CPU (the reference's eager PyTorch path on the host cores; rank 0 only)",
                 "cpu_baseline": {"value": round(v, 1), "unit": "ms/step", "cores": cores, "kind": "port",
-                                 "sample": sample},
+                                 "sample": sample, "spread": round((max(runs) - min(runs)) / v, 3),
+                                 "runs_ms_min_max": [round(min(runs), 1), round(max(runs), 1)]},
                 "e2e": {"value": round(v, 1), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
