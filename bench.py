@@ -471,6 +471,42 @@ def gemm_roofline(spans, pk, src, shapes=None, in_step=False):
             "work_per_step": g["work"], "launches_per_step": g["calls"], "ms_per_step": round(g["ms"], 3)}
 
 
+def int8_library_rate(dev, sustained_s=1.5):
+    """The INT8 tensor rate of the box's own library GEMM, measured here:
+    torch._int_mm (cuBLASLt, int8 x int8 -> int32, no epilogue) at 8192^3 --
+    "burst": the best of 10 launches timed alone; "sustained": back to back for
+    about sustained_s seconds (power-capped clocks, like a GEMM inside the
+    step).  A reference beside the 2 x bf16 figure, which is inferred."""
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(2)
+    a = torch.randint(-127, 128, (n, n), generator=g, dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), generator=g, dtype=torch.int8, device=dev)
+    ops = 2.0 * n ** 3
+    for _ in range(3):
+        torch._int_mm(a, b.t())
+    best = None
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b.t())
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    reps = max(1, int(sustained_s * 1e3 / best))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        torch._int_mm(a, b.t())
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sus = e0.elapsed_time(e1) / reps
+    del a, b
+    torch.cuda.empty_cache()
+    return {"gemm": "torch._int_mm (cuBLASLt) 8192^3 int8 -> int32", "burst_tops": round(ops / best / 1e9, 1),
+            "sustained_tops": round(ops / sus / 1e9, 1), "sustained_launches": reps}
+
+
 def breakdown(spans, pk):
     out = {}
     for name, d in sorted(spans.items()):
@@ -1075,6 +1111,12 @@ def main():
                                               in_step=True),
                     "clocks": r["clocks"], "e2e": r["e2e"], "parity": r["parity"],
                     "gpu_launches": int(round(r["launches"] * args.steps)), "breakdown": breakdown(spans, pk)}
+            rl = line["roofline"]
+            if rl is not None:
+                # the GEMM against a measured INT8 rate of this GPU as well (cuBLASLt, timed after the timed regions)
+                lib = int8_library_rate(dev)
+                rl["int8_library_measured"] = lib
+                rl["frac_of_library_sustained"] = round(rl["achieved"] / lib["sustained_tops"], 4)
             if rank == 0 and world == 1 and not args.no_cpu_baseline and not step_cfg:
                 line["cpu_baseline"] = cpu_baseline(cfg, seq)
             if not step_cfg and world > 1 and not args.no_a2a:
