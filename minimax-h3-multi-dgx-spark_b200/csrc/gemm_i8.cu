@@ -20,9 +20,10 @@
 //               while this one drains.
 // Tiles are visited in the reference's grouped-M order (int8_gemm_triton.py:37-45,
 // GROUP_M = 8 there; 16 tile rows per group here, chosen by measurement) so
-// CTAs running at the same time share A and B rows in L2.  Every mbarrier wait is bounded; on expiry the kernel records
-// H3B_STATUS_MBAR_TIMEOUT, stops issuing work, drains its own TMA loads and
-// MMAs (again bounded), frees TMEM and returns.
+// CTAs running at the same time share A and B rows in L2.  Every mbarrier wait
+// is bounded; on expiry the kernel records H3B_STATUS_MBAR_TIMEOUT, stops
+// issuing work, drains its own TMA loads and MMAs (again bounded), frees TMEM
+// and returns.
 #include <mutex>
 #include <cuda.h>
 #include <stdlib.h>
@@ -846,6 +847,21 @@ static int num_sms() {
     return sms;
 }
 
+// Tile rows per group of the grouped-M raster (the weights are streamed once
+// per group): GROUP_M = 16, measured on the block's four shapes at M=128000
+// 2-4% faster than 8 on each (the weights are streamed half as often) and
+// faster than 32 (whose A slabs no longer stay in L2 for K=13824).
+// H3B_GEMM_GROUP_M overrides it for tuning sweeps.
+static int pick_group_m() {
+    static int forced = -1;
+    if (forced < 0) {
+        const char* e = getenv("H3B_GEMM_GROUP_M");
+        const int v = e ? atoi(e) : 0;
+        forced = (v >= 1 && v <= 256) ? v : 0;
+    }
+    return forced ? forced : GROUP_M;
+}
+
 // Output tile width of the 2-CTA kernel.  The kernel is bound by the L2->SM
 // feed (measured: throughput at width t scales as 1 / (8192/t + 32) bytes per
 // clock per SM), so a tile's run time is proportional to the operand rows it
@@ -853,23 +869,6 @@ static int num_sms() {
 // (rounds of pair tiles over the resident pairs) x (256 + t); ties go to the
 // wider tile.  Wave quantisation picks 224 for config 0's 4096 x 5120; large M
 // keeps 256.
-// Tile rows per group of the grouped-M raster (the weights are streamed once
-// per group).  H3B_GEMM_GROUP_M overrides it for tuning sweeps.
-static int pick_group_m(int K) {
-    static int forced = -1;
-    if (forced < 0) {
-        const char* e = getenv("H3B_GEMM_GROUP_M");
-        const int v = e ? atoi(e) : 0;
-        forced = (v >= 1 && v <= 256) ? v : 0;
-    }
-    if (forced) return forced;
-    // 16 tile rows per group: measured on the block's four shapes at M=128000,
-    // 2-4% faster than 8 on each (the weights are streamed half as often) and
-    // faster than 32 (whose A slabs no longer stay in L2 for K=13824)
-    (void)K;
-    return GROUP_M;
-}
-
 static int pick_tile_n(int M, int N, int64_t pairs, int multiple = 32) {
     // H3B_GEMM_TILE_N (a multiple of 32 in 32..256) pins the width, for tuning sweeps
     static int forced = -1;
@@ -951,7 +950,7 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
         H3B_REQUIRE(!a.bias || aligned(a.bias, 16), "h3b GEMM: bias must be 16-byte aligned");
     }
     if (a.M == 0) return H3B_OK;
-    a.group_m = pick_group_m(a.K);
+    a.group_m = pick_group_m();
     if (int rc = check_device()) return rc;
     CUtensorMap tmA, tmB;
     if (int rc = make_map(&tmA, xq, a.M, a.K, BM)) return rc;
