@@ -315,7 +315,10 @@ class HostPipeline:
                 self.copy_in.wait_event(self.freed[i])
             self._timed_copy("in", self.copy_in, slot, x_host)
             if cond_host is not None:
-                if self.cond_slots[i] is None:
+                have = self.cond_slots[i]
+                if have is None or len(have) != len(cond_host) or any(
+                        d.shape != c.shape or d.dtype != c.dtype for d, c in zip(have, cond_host)):
+                    # first use of the slot, or conditioning of another shape: its own device buffers
                     self.cond_slots[i] = [torch.empty(c.shape, dtype=c.dtype, device=self.device) for c in cond_host]
                 cond_dev = self.cond_slots[i]
                 for d, c in zip(cond_dev, cond_host):
