@@ -169,22 +169,34 @@ __global__ void __launch_bounds__(128) gate_kernel(uint16_t* __restrict__ x, con
 // h (the quantiser fused into its producer).
 constexpr int kNorm8Threads = 64;
 
-__device__ __forceinline__ uint32_t norm2(uint32_t xp, float rstd, uint32_t wp, uint32_t sp, uint32_t hp) {
-    const uint32_t y = pack_bf16x2(__fmul_rn(bf16_lo(wp), __fmul_rn(rstd, bf16_lo(xp))),
-                                   __fmul_rn(bf16_hi(wp), __fmul_rn(rstd, bf16_hi(xp))));
-    const uint32_t z = pack_bf16x2(__fmul_rn(bf16_lo(y), bf16_lo(sp)), __fmul_rn(bf16_hi(y), bf16_hi(sp)));
-    return pack_bf16x2(__fadd_rn(bf16_lo(z), bf16_lo(hp)), __fadd_rn(bf16_hi(z), bf16_hi(hp)));
+// The bf16 pair of a 32-bit word as an f32x2 operand (lane 0 = bits 0-15).
+__device__ __forceinline__ uint64_t bf2(uint32_t v) { return f2(bf16_lo(v), bf16_hi(v)); }
+
+// bf16 pair from an f32x2 value, each lane rounded to nearest even
+__device__ __forceinline__ uint32_t rbf2(uint64_t v) {
+    float a, b;
+    f2_split(v, a, b);
+    return pack_bf16x2(a, b);
+}
+
+// The per-element arithmetic below runs on fp32 pairs (f32x2 instructions
+// round each lane exactly as the scalar __fmul_rn / __fadd_rn would), two
+// elements per instruction; the rounding points are unchanged.
+__device__ __forceinline__ uint32_t norm2(uint32_t xp, uint64_t rstd2, uint32_t wp, uint32_t sp, uint32_t hp) {
+    const uint32_t y = rbf2(mul2(bf2(wp), mul2(rstd2, bf2(xp))));
+    const uint32_t z = rbf2(mul2(bf2(y), bf2(sp)));
+    return rbf2(add2(bf2(z), bf2(hp)));
 }
 
 // Plain RMSNorm with weight (no modulation): rbf16(w * (rstd * x)), the first
 // rounding point of norm2 -- F.rms_norm's output.
-__device__ __forceinline__ uint32_t rms2(uint32_t xp, float rstd, uint32_t wp) {
-    return pack_bf16x2(__fmul_rn(bf16_lo(wp), __fmul_rn(rstd, bf16_lo(xp))),
-                       __fmul_rn(bf16_hi(wp), __fmul_rn(rstd, bf16_hi(xp))));
+__device__ __forceinline__ uint32_t rms2(uint32_t xp, uint64_t rstd2, uint32_t wp) {
+    return rbf2(mul2(bf2(wp), mul2(rstd2, bf2(xp))));
 }
 
+// x + o * g: the bf16 product is exact in fp32, the sum rounds once (gate1)
 __device__ __forceinline__ uint32_t gate2(uint32_t xp, uint32_t op, uint32_t gp) {
-    return pack_bf16x2(gate1(bf16_lo(xp), bf16_lo(op), bf16_lo(gp)), gate1(bf16_hi(xp), bf16_hi(op), bf16_hi(gp)));
+    return rbf2(add2(bf2(xp), mul2(bf2(op), bf2(gp))));
 }
 
 __device__ __forceinline__ float sumsq2(uint32_t v, float acc) {
@@ -255,6 +267,7 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
     __syncthreads();
     const float tot = __fadd_rn(__fadd_rn(wsum[0], wsum[2]), __fadd_rn(wsum[1], wsum[3]));
     const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.D), a.eps));
+    const uint64_t rstd2 = f2(rstd, rstd);
 
     const uint4* wv = reinterpret_cast<const uint4*>(a.w);
     const bool modulate = a.s1 != nullptr;
@@ -270,11 +283,11 @@ __global__ void __launch_bounds__(kNorm8Threads) norm8_kernel(NormArgs a, int8_t
             uint4 y;
             if (modulate) {
                 const uint4 s4 = s1r[j], h4 = shr[j];
-                y = make_uint4(norm2(v[it].x, rstd, w4.x, s4.x, h4.x), norm2(v[it].y, rstd, w4.y, s4.y, h4.y),
-                               norm2(v[it].z, rstd, w4.z, s4.z, h4.z), norm2(v[it].w, rstd, w4.w, s4.w, h4.w));
+                y = make_uint4(norm2(v[it].x, rstd2, w4.x, s4.x, h4.x), norm2(v[it].y, rstd2, w4.y, s4.y, h4.y),
+                               norm2(v[it].z, rstd2, w4.z, s4.z, h4.z), norm2(v[it].w, rstd2, w4.w, s4.w, h4.w));
             } else {
-                y = make_uint4(rms2(v[it].x, rstd, w4.x), rms2(v[it].y, rstd, w4.y), rms2(v[it].z, rstd, w4.z),
-                               rms2(v[it].w, rstd, w4.w));
+                y = make_uint4(rms2(v[it].x, rstd2, w4.x), rms2(v[it].y, rstd2, w4.y), rms2(v[it].z, rstd2, w4.z),
+                               rms2(v[it].w, rstd2, w4.w));
             }
             if constexpr (Q8) {
                 v[it] = y;
