@@ -306,7 +306,7 @@ def dit_workload(args, rank, world, dev, n_blocks, seq, text_len, steps, warmup,
         if args.exchange == "p2p":
             peer = h3b.PeerExchange(dist.group.WORLD, rank, world, seq, cfg.heads, cfg.head_dim)
         ctx = h3b.SPContext(rank, world, dist.group.WORLD, seq, exchange=args.exchange, peer=peer)
-        h3b.startup_probe(rank, world, dist.group.WORLD, dev)
+        h3b.startup_probe(rank, world, dist.group.WORLD, dev, peer=peer)
         start, stop = ctx.start, ctx.stop
     else:
         start, stop = 0, seq

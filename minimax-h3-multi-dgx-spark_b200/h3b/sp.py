@@ -8,7 +8,8 @@ Mirrors comfyui_nodes/minimax-h3-sp/minimax_sp/sp_forward.py:
   sp_attention_overlap(q, k, v, ctx, ...)   :211-261  exchange/attention overlap by head groups
   overlap_groups(hp, world)                 :58,264-273
   gather_rows(local, counts, ctx, out_dim)  :378-389  padded all-gather of the final rows
-and the known-answer start-up probe of sp_group.py:107-128.
+and the known-answer start-up probe of sp_group.py:107-128 (for the NCCL group
+and, given a PeerExchange, for the peer-memory back end).
 
 Two exchange back ends, chosen per SPContext (`ctx.exchange`):
   * "nccl": pack kernel -> grouped NCCL send/recv (torch.distributed
@@ -524,10 +525,12 @@ def gather_rows(local, counts, ctx, out_dim, device=None):
 
 # ---------------------------------------------------------------------------
 
-def startup_probe(rank, world, group, device):
+def startup_probe(rank, world, group, device, peer=None):
     """Known-answer check of the tensor process group (sp_group.py:107-128):
     all_reduce of rank+1 sums to P(P+1)/2 and all_to_all_single of
-    arange(P) + rank*P returns arange(P)*P + rank."""
+    arange(P) + rank*P returns arange(P)*P + rank.  With `peer` (a
+    PeerExchange) the peer-memory back end is checked the same way
+    (probe_peer).  Collective: every rank of the group calls it."""
     reduced = torch.tensor([rank + 1], dtype=torch.float32, device=device)
     dist.all_reduce(reduced, group=group)
     expected_sum = world * (world + 1) / 2
@@ -539,3 +542,35 @@ def startup_probe(rank, world, group, device):
     expected = torch.arange(world, dtype=torch.int64, device=device) * world + rank
     if not torch.equal(received, expected):
         raise RuntimeError(f"all_to_all_single returned {received.tolist()}, expected {expected.tolist()}")
+    if peer is not None:
+        probe_peer(peer, rank, world, group, device)
+
+
+def _probe_values(rows, cols):
+    """(row * 7 + column) % 251: integers below 256, exact in bf16."""
+    return ((rows[:, None] * 7 + cols[None, :]) % 251).to(torch.bfloat16)
+
+
+def probe_peer(peer, rank, world, group, device):
+    """Known-answer round trip through the peer-memory back end, the p2p
+    counterpart of the reference's start-up probe: each rank's rows of an
+    [S, H, Dh] tensor of known values (S uneven over the ranks when the
+    buffers allow) go through the forward exchange -- every rank must receive
+    its heads of every row -- and the received rows back through the inverse
+    -- every rank must get its own rows.  A mismatch on any rank raises on
+    every rank (the verdict is all-reduced).  Collective."""
+    H, Dh = peer.heads, peer.head_dim
+    S = min(peer.seq_len, 16 * world + world - 1)
+    ctx = SPContext(rank, world, group, S, exchange="p2p", peer=peer)
+    cols = torch.arange(H * Dh, device=device, dtype=torch.int64)
+    t = _probe_values(torch.arange(ctx.start, ctx.stop, device=device, dtype=torch.int64), cols).view(-1, H, Dh)
+    got = peer.fwd([t], ctx)[0].reshape(S, -1)
+    hp = H // world
+    want = _probe_values(torch.arange(S, device=device, dtype=torch.int64), cols[rank * hp * Dh:(rank + 1) * hp * Dh])
+    ok = torch.equal(got, want)
+    back = peer.inv(got, ctx)
+    ok = ok and torch.equal(back.reshape(ctx.local, -1), t.reshape(ctx.local, -1))
+    bad = torch.tensor([0 if ok else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(bad, group=group)
+    if bad.item():
+        raise RuntimeError(f"peer-memory exchange probe failed on {bad.item()} of {world} ranks")

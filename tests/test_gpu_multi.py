@@ -78,6 +78,7 @@ def _worker(rank, world, port, q):
             mine = [ins[i][rank].to(dev) for i in range(3)]
             o_mine = outs[rank].to(dev)
             peer = h3b.PeerExchange(g, rank, world, S, H, Dh)
+            h3b.startup_probe(rank, world, g, dev, peer=peer)  # the p2p known-answer round trip
             for exch in ("nccl", "p2p"):
                 ctx = h3b.SPContext(rank, world, g, S, exchange=exch, peer=peer if exch == "p2p" else None)
                 for rep in range(2):  # twice: the p2p buffers and flags are reused
