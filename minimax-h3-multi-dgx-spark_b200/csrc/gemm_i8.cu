@@ -552,8 +552,20 @@ constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = B_ROWS * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr int kStagingBytes = kEpiWarps * 32 * 128;  // scatter epilogue: 32 rows x 128 B per warp
+// Epilogue warps.  The plain variant has two per TMEM lane quarter (warps w
+// and w + 4 read the same 32 accumulator rows and take alternate 32-column
+// chunks), so the dequantisation (and the GELU) of one accumulator runs on
+// eight warps while the MMAs fill the other.  The scatter variant keeps one
+// per quarter: its q/k-norm epilogue holds a whole 128-column head per thread
+// (255 registers); at 320 threads, capped at 200 registers, it spilled and its
+// launch was refused for resources.
+template <bool SCATTER>
+constexpr int epi_warps() { return SCATTER ? 4 : 8; }
+template <bool SCATTER>
+constexpr int threads() { return 64 + 32 * epi_warps<SCATTER>(); }  // TMA producer, MMA issuer, epilogue
+constexpr int kStagingBytes = epi_warps<true>() * 32 * 128;  // scatter epilogue: 32 rows x 128 B per warp
 constexpr int kSmemBytesScatter = kSmemBytes + kStagingBytes;
+static_assert(kSmemBytesScatter <= 227 * 1024, "shared memory of the scatter variant above the 227 KB per CTA");
 // instruction descriptor without its N field (bits 17-22 = N >> 3, set per launch)
 constexpr uint32_t kIdescBase = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TILE_M >> 4) << 24);
 
@@ -600,7 +612,7 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 }
 
 template <bool OUT_I32, bool SCATTER>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads<SCATTER>(), 1)
     gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args args) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -626,7 +638,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < NUM_ACC; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 2 * kEpiWarps);
+            mbar_init(&tempty[a], 2 * epi_warps<SCATTER>());
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -747,8 +759,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue warps 2..5 (both CTAs: rows rank*128 .. of the pair tile)
-        const int q = warp & 3;
+        // ---------------- epilogue warps 2 .. (both CTAs: rows rank*128 .. of the pair tile)
+        const int q = warp & 3;                                        // TMEM lane quarter of this warp
+        const int ew = warp - 2;                                       // epilogue warp index
+        const int part = ew >> 2, nparts = epi_warps<SCATTER>() / 4;  // this warp's share of the columns
         int t = 0;
         for (int tile = pair_id; tile < num_tiles; tile += n_pairs, ++t) {
             int mb, nb;
@@ -764,25 +778,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * MAX_TILE_N);
             if constexpr (SCATTER) {
                 // 64-column units (TILE_N % 64 == 0 and N % 64 == 0 for this variant)
-                uint4* stage = reinterpret_cast<uint4*>(base + STAGES * STAGE_BYTES + 256) + q * (32 * 8);
+                uint4* stage = reinterpret_cast<uint4*>(base + STAGES * STAGE_BYTES + 256) + ew * (32 * 8);
+                // items: 64-column units, or whole 128-column heads when normalised
+                // (tile_n % 128 == 0 then); with two warps per lane quarter they
+                // take alternate items
 #pragma unroll 1
-                for (int c = 0; c < TILE_N / 64;) {
+                for (int c = 0, item = 0; c < TILE_N / 64; ++item) {
                     const int col0 = nb * TILE_N + c * 64;
                     if (col0 >= N) break;  // warp-uniform
                     const int t = col0 / args.sc.seg;
-                    if (t < args.sc.norm_segs) {
-                        // a whole 128-column head (tile_n % 128 == 0 for this case)
-                        scatter_head_norm(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane,
-                                          args.sc.norm_w + t * 128);
-                        c += 2;
-                    } else {
-                        scatter_unit(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane);
-                        ++c;
+                    const bool norm = t < args.sc.norm_segs;
+                    if (item % nparts == part) {
+                        if (norm)
+                            scatter_head_norm(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane,
+                                              args.sc.norm_w + t * 128);
+                        else
+                            scatter_unit(args, stage, t_row + (uint32_t)(c * 64), row - lane, col0, xs, lane);
                     }
+                    c += norm ? 2 : 1;
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < TILE_N / 32; ++c) {
+                for (int c = part; c < TILE_N / 32; c += nparts) {
                     const int col0 = nb * TILE_N + c * 32;
                     if (col0 >= N) break;  // warp-uniform
                     uint32_t r[32];
@@ -918,7 +935,7 @@ static int max_pairs() {
     int n = 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(pair::threads<SCATTER>(), 1, 1);
     cfg.dynamicSmemBytes = SCATTER ? pair::kSmemBytesScatter : pair::kSmemBytes;
     if (cudaOccupancyMaxActiveClusters(&n, (void*)pair::gemm_i8_pair_kernel<OUT_I32, SCATTER>, &cfg) != cudaSuccess ||
         n <= 0) {
@@ -969,7 +986,7 @@ static int launch(const int8_t* xq, const int8_t* w, Args a, cudaStream_t s) {
         if (int rc = make_map(&tmB, w, a.N, a.K, (uint32_t)(a.tile_n / 2))) return rc;
         const int64_t tiles = (int64_t)((a.M + pair::TILE_M - 1) / pair::TILE_M) * ((a.N + a.tile_n - 1) / a.tile_n);
         const int pairs = (int)(tiles < pairs_max ? tiles : pairs_max);
-        pair::gemm_i8_pair_kernel<OUT_I32, SCATTER><<<2 * pairs, kThreads, smem, s>>>(tmA, tmB, a);
+        pair::gemm_i8_pair_kernel<OUT_I32, SCATTER><<<2 * pairs, pair::threads<SCATTER>(), smem, s>>>(tmA, tmB, a);
     } else {
         H3B_CUDA_TRY(cudaFuncSetAttribute(gemm_i8_kernel<OUT_I32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         const int64_t tiles = (int64_t)((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN);
