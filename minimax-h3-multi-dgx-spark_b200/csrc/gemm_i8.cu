@@ -12,7 +12,8 @@
 //               thread: 4 x tcgen05.mma M=128 N=256 K=32 per stage into one
 //               of two 256-column int32 accumulators; tcgen05.commit frees the
 //               stage and, after the last k-block, hands the accumulator over.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
+//   warps 2..    epilogue (4 warps; 8 in the plain 2-CTA variant, two per lane
+//               quarter): tcgen05.ld 32 columns at a time (warp w reads TMEM
 //               lanes 32*(w%4)..+31 = tile rows), dequantise with separate
 //               IEEE multiplies (no FMA contraction: the reference rounds
 //               after each product), round once to bf16, store; then release
