@@ -74,3 +74,25 @@ def test_matches_a_literal_restatement_on_random_tilings():
             expect += row.tolist() if torch.is_tensor(row) else [row] * (b - a)
         r = row_index(shuffled, s, CPU)
         assert r is not None and r.tolist() == expect
+
+
+def test_modulation_tables_match_the_oracle():
+    """The six tables of a7 (h3_fuse_patch.py:111-118): s1 = bf16(1.0 + bf16(scale)),
+    shift and gate rounded to bf16, against the C oracle's scalar restatement,
+    on values that straddle bf16 rounding boundaries after the 1.0 is added."""
+    import numpy as np
+    oracle = pytest.importorskip("oracle")
+    g = torch.Generator().manual_seed(5)
+    D = 4096
+    e = torch.randn(6, D, generator=g) * 0.1
+    # scale values whose bf16 sum with 1.0 lands on or next to a tie, tiny and large magnitudes, -1
+    e[1, :8] = torch.tensor([2 ** -9, -2 ** -9, 3 * 2 ** -9, 2 ** -30, -1.0, 300.0, -2 ** -8, 1e-3])
+    e[4, :4] = torch.tensor([2 ** -9 + 2 ** -17, -0.75, 65504.0, -1e-8])
+    tabs = h3b.modulation_tables(*(e[i] for i in range(6)))
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    rne = lambda t: oracle.f32_to_bf16(t.numpy())  # noqa: E731
+    s1a, sha, ga, s1m, shm, gm = (bits(t) for t in tabs)
+    np.testing.assert_array_equal(s1a, oracle.one_plus(rne(e[1]), oracle.RNE))
+    np.testing.assert_array_equal(s1m, oracle.one_plus(rne(e[4]), oracle.RNE))
+    for got, i in ((sha, 0), (ga, 2), (shm, 3), (gm, 5)):
+        np.testing.assert_array_equal(got, rne(e[i]))
